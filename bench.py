@@ -1,0 +1,384 @@
+#!/usr/bin/env python
+"""Benchmark of the attention hot path on the configuration BASELINE's metric is quoted on (config 2):
+decode attention of 28 layers x 64 takes per GPU, 16 q / 2 kv heads, hd 128, bf16 KV slots of 4096 positions,
+per-take lengths uniform in [330, 4096], one query per take per layer, all layers in one captured CUDA graph.
+
+One step = for each of the 28 layers: the decode prologue (rope of q/k at each take's position + k/v written into the
+take's slot) and the split-KV decode attention with the combine fused — two launches per layer.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+For N > 1 it runs under torchrun, one rank per GPU; every rank owns its own 64 takes (takes are independent,
+no collective on the data path), so scaling is weak. Rank 0 prints one JSON line.
+--impl reference times the reference algorithm's CPU restatement (oracle/, all host threads) on the same workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode-attn HBM GB/s (% of 8 TB/s) at 64 takes×KV4096; patches/sec at 1/2/4/8 B200"
+NQ, NK, HD, MAXLEN, LAYERS, TAKES = 16, 2, 128, 4096, 28, 64
+LEN_LO, LEN_HI = 330, 4096
+NOMINAL_HBM_GBS = 8000.0
+WORKLOAD = ("config 2: decode attention, 28 layers x 64 takes per GPU, 16 q / 2 kv heads, hd 128, bf16 KV slots "
+            "of 4096, per-take lengths U[330,4096], one query per take per layer, one CUDA graph per step")
+
+
+def take_lengths(rank):
+    from oumu_b200 import synth
+    return synth.uniform_int(synth.config_seed(1) + 1000 * rank, TAKES, LEN_LO, LEN_HI)
+
+
+def bytes_per_layer(lens):
+    """Algorithmic bytes of one layer's decode attention: K and V of the L_s valid positions of each take, its
+    q heads read and its output written (2*nk*L*hd*2 + 2*nq*hd*2 per take)."""
+    return int(sum(2 * NK * int(L) * HD * 2 + 2 * NQ * HD * 2 for L in lens))
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def committed_traffic():
+    """DRAM bytes per attention launch from the committed ncu summary (profiles/), scaled to one full launch."""
+    p = os.path.join(ROOT, "profiles", "decode_attn_config2.md")
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """SM clock and clock-event reasons sampled with NVML every 10 ms while active (read-only queries)."""
+
+    REASONS = {0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x4: "sw_power_cap",
+               0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.ok = [], set(), False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            uuid = None
+            try:
+                import torch
+                uuid = "GPU-" + str(torch.cuda.get_device_properties(index).uuid)
+            except Exception:
+                pass
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid) if uuid else pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # no NVML: the line says so
+            self.err = str(e)
+
+    def _run(self):
+        nv = self.nv
+        while not self.stop:
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self.ok:
+            self.stop = False
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self.stop = True
+            self.t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": getattr(self, "err", "no samples")}
+        return {"sm_mhz": float(statistics.median(self.samples)), "sm_max_mhz": float(self.max_mhz),
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------------------------------------------------
+# CPU leg: the reference algorithm's fp32 restatement (oracle/) on the host cores
+# ------------------------------------------------------------------------------------------------------------
+
+def cpu_inputs(lens, layers, seed):
+    from oumu_b200 import synth
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(layers):
+        qkv = synth.f32_to_bf16(rng.standard_normal((TAKES, (NQ + 2 * NK) * HD), dtype=np.float32))
+        kc = np.zeros((TAKES, NK, MAXLEN, HD), np.uint16)
+        vc = np.zeros_like(kc)
+        for s, L in enumerate(lens):  # only the valid positions are read
+            kc[s, :, :L] = synth.f32_to_bf16(rng.standard_normal((NK, L, HD), dtype=np.float32))
+            vc[s, :, :L] = synth.f32_to_bf16(rng.standard_normal((NK, L, HD), dtype=np.float32))
+        out.append((qkv, kc, vc))
+    return out
+
+
+def cpu_time(lens, layers, min_seconds):
+    """Times the oracle's decode attention over `layers` layers of the workload until min_seconds have passed;
+    returns (GB/s, threads, seconds, sample description)."""
+    from oracle import cpu
+    data = cpu_inputs(lens, layers, 7)
+    ln = np.asarray(lens, np.int32)
+    nbytes, reps, t0 = 0, 0, time.perf_counter()
+    while True:
+        for qkv, kc, vc in data:
+            cpu.attn_decode(qkv, kc, vc, None, ln, TAKES, NQ, NK, HD, MAXLEN, HD ** -0.5)
+            nbytes += bytes_per_layer(lens)
+        reps += 1
+        dt = time.perf_counter() - t0
+        if dt >= min_seconds:
+            break
+    return nbytes / dt / 1e9, cpu.threads(), dt, f"{reps} x {layers} layer(s) x {TAKES} takes of config 2"
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    from oracle import cpu
+    lens = take_lengths(0)
+    data = cpu_inputs(lens, 1, 7)
+    qkv, kc, vc = data[0]
+    ln = np.asarray(lens, np.int32)
+    group = 8  # takes per step: each step is a bounded sample of the workload, rotating over the 64 takes
+
+    def one(i):
+        s0 = (i * group) % TAKES
+        sl = slice(s0, s0 + group)
+        cpu.attn_decode(qkv[sl], kc[sl], vc[sl], None, ln[sl], group, NQ, NK, HD, MAXLEN, HD ** -0.5)
+        return bytes_per_layer(lens[sl])
+
+    for i in range(args.warmup):
+        one(i)
+    nbytes, t0 = 0, time.perf_counter()
+    for i in range(args.steps):
+        nbytes += one(args.warmup + i)
+    dt = time.perf_counter() - t0
+    gbs = nbytes / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * dt / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) bf16 q/k/v, per-take lengths U[330,4096])",
+        "config": {"workload": WORKLOAD, "takes_per_gpu": TAKES, "layers": LAYERS, "maxlen": MAXLEN},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cpu.threads(), "kind": "port",
+                         "sample": f"each step: one layer of {group} of the 64 takes (rotating), fp32 C "
+                                   "restatement of kernels/voxcpm.cu:131-185 (OpenMP)"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference implements this path only as CUDA kernels; its CPU form is the oracle port",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------------------------------------
+# GPU arm
+# ------------------------------------------------------------------------------------------------------------
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    from oumu_b200 import build, ops
+    if rank == 0 or world == 1:
+        build.build()
+    if world > 1:
+        dist.barrier()
+    lens = take_lengths(rank)
+    W = (NQ + 2 * NK) * HD
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0x5EED + 1 + rank)
+
+    def rnd(*shape):
+        return torch.randn(shape, generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
+
+    qkv_all = rnd(LAYERS, TAKES, W)
+    kc = [rnd(TAKES, NK, MAXLEN, HD) for _ in range(LAYERS)]
+    vc = [rnd(TAKES, NK, MAXLEN, HD) for _ in range(LAYERS)]
+    att_all = torch.zeros((LAYERS, TAKES, NQ * HD), dtype=torch.bfloat16, device=dev)
+    cs, sn = ops.rotary_tables(MAXLEN, HD)
+    cs, sn = cs.to(dev), sn.to(dev)
+    ln = torch.tensor(lens, dtype=torch.int32, device=dev)
+    ws = ops.decode_workspace(TAKES, NQ, NK, HD, MAXLEN, dev)
+    per_layer = bytes_per_layer(lens)
+    per_step = LAYERS * per_layer
+
+    def step():
+        for l in range(LAYERS):
+            ops.step_tf_attention(qkv_all[l], kc[l], vc[l], att_all[l], ws, cs, sn, None, ln, TAKES, NQ, NK, HD,
+                                  MAXLEN)
+
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        step()  # eager once (first-use set-up outside the capture)
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    # ---- device-resident timing ----
+    t_end = time.perf_counter() + 0.3
+    while time.perf_counter() < t_end:  # let the clocks settle (untimed)
+        graph.replay()
+        torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        graph.replay()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    barrier()
+    total_bytes = sum_over_ranks(per_step * args.steps)
+    value = total_bytes / (ms / 1e3) / 1e9
+
+    # ---- dominant kernel: the attention launch alone, CUDA events on the launching stream ----
+    reps = max(2, min(10, args.steps // 20))
+    durs = []
+    for _ in range(reps):
+        for l in range(LAYERS):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            ops.attn_decode(qkv_all[l], kc[l], vc[l], att_all[l], ws, None, ln, TAKES, NQ, NK, HD, MAXLEN,
+                            HD ** -0.5)
+            b.record()
+            durs.append((a, b))
+    torch.cuda.synchronize()
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in durs)
+    kern_ms = max_over_ranks(kern_ms)
+    achieved = per_layer / (kern_ms / 1e3) / 1e9
+    peak, peak_kind = measured_peak()
+    traffic = committed_traffic()
+
+    # ---- end to end through the C ABI: host qkv in, host attention out, every step ----
+    qkv_host = torch.empty_like(qkv_all, device="cpu").pin_memory()
+    qkv_host.copy_(qkv_all)
+    att_host = torch.empty_like(att_all, device="cpu").pin_memory()
+    h2d, d2h = qkv_all.numel() * 2, att_all.numel() * 2
+    for _ in range(args.warmup):
+        qkv_all.copy_(qkv_host, non_blocking=True)
+        graph.replay()
+        att_host.copy_(att_all, non_blocking=True)
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        qkv_all.copy_(qkv_host, non_blocking=True)
+        graph.replay()
+        att_host.copy_(att_all, non_blocking=True)
+    f1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1))
+    e2e_value = total_bytes / (e2e_ms / 1e3) / 1e9
+    errword = ops.device_error()
+    barrier()
+
+    cpu_base = None
+    if world == 1 and not args.no_cpu:
+        gbs, thr, secs, sample = cpu_time(lens, 2, 10.0)
+        cpu_base = {"value": round(gbs, 3), "unit": "GB/s", "cores": thr, "kind": "port",
+                    "sample": f"{sample} ({secs:.1f} s), fp32 C restatement of kernels/voxcpm.cu:131-185"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) bf16 q/k/v, per-take lengths U[330,4096])",
+            "config": {"workload": WORKLOAD, "takes_per_gpu": TAKES, "layers": LAYERS, "maxlen": MAXLEN,
+                       "mean_len": float(np.mean(lens)), "bytes_per_step_per_gpu": per_step,
+                       "l2": "inputs larger than L2 (3.7 GB of K/V per step per GPU)",
+                       "parallelism": f"takes sharded over {world} GPU(s), no collective on the data path"},
+            "pct_of_8TBps_per_gpu": round(100 * value / world / NOMINAL_HBM_GBS, 2),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "peak_kind": peak_kind, "kernel": "dec::k_attn_decode<128>",
+                         "kernel_ms": round(kern_ms, 5), "algorithmic_bytes_per_launch": per_layer},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / args.steps, 4),
+                    "path": "pinned host qkv -> device, graph of C-ABI calls, attention output -> pinned host"},
+            "cpu_baseline": cpu_base,
+            "clocks": clocks.summary(),
+            "gpu_launches": 2 * LAYERS * args.steps,
+            "device_error": errword,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

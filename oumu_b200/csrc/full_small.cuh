@@ -1,0 +1,141 @@
+// Attention inside many short independent sequences (seq <= 16): the LocDiT passes (11 or 12 tokens, all takes x
+// both CFG branches in one launch) and the local encoder (5 tokens).
+//
+// One warp per (sequence, q head) unit, persistent over units. The warp stages its q, k and v rows (16-byte
+// cp.async, 128-byte-swizzled rows, padding rows zeroed) in its own shared-memory slice, then on tensor cores:
+//   S[16 x 16] = Q[16 x hd] . K^T          (mma.sync m16n8k16, fp32 accumulate)
+//   row softmax in fp32 (exp2 with the scale folded), masked keys (>= seq, or causal) -> 0
+//   O[16 x hd] = P . V                       (P split as bf16 hi + lo, so the weights keep ~16 mantissa bits)
+//   out = bf16(O * (1 / sum))                the reference's normalisation point (kernels/voxcpm.cu:291-295)
+#pragma once
+#include "common.cuh"
+
+namespace fs {
+
+constexpr int WARPS = 4;
+constexpr int ROWS = 16;
+
+template <int HD>
+struct Cfg {
+    static constexpr int NBOX = HD / 64;
+    static constexpr int MAT_BYTES = NBOX * ROWS * 128;   // one 16-row matrix, 128-B swizzled rows per box
+    static constexpr int WARP_BYTES = 3 * MAT_BYTES;      // q, k, v
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+template <int HD>
+__global__ void __launch_bounds__(WARPS * 32) k_attn_small(const bf16 *__restrict__ qkv, bf16 *__restrict__ out,
+                                                           int nseq, int seq, int causal, int nq, int nk,
+                                                           float sl2) {
+    using C = Cfg<HD>;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t *ws = smem + warp * C::WARP_BYTES;
+    const uint32_t ws_s = smem_u32(ws);
+    const int stride = (nq + 2 * nk) * HD, G = nq / nk;
+    const int CPR = HD / 8;  // 16-byte chunks per row
+    const long units = static_cast<long>(nseq) * nq;
+    const int r4 = lane >> 2, c2 = (lane & 3) * 2, mi = lane >> 3;
+
+    for (long u = static_cast<long>(blockIdx.x) * WARPS + warp; u < units; u += static_cast<long>(gridDim.x) * WARPS) {
+        const int n = static_cast<int>(u / nq), h = static_cast<int>(u % nq), kh = h / G;
+        const bf16 *base = qkv + static_cast<long>(n) * seq * stride;
+        // ---- stage q, k, v rows (rows >= seq zero-filled) ----
+        for (int i = lane; i < 3 * ROWS * CPR; i += 32) {
+            const int mat = i / (ROWS * CPR), rem = i % (ROWS * CPR), r = rem / CPR, ch = rem % CPR;
+            const uint32_t dst = ws_s + mat * C::MAT_BYTES + (ch >> 3) * (ROWS * 128) + sw128(r, ch & 7);
+            if (r < seq) {
+                const int col = mat == 0 ? h * HD : (mat == 1 ? (nq + kh) * HD : (nq + nk + kh) * HD);
+                cp_async16(dst, base + static_cast<long>(r) * stride + col + ch * 8);
+            } else {
+                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0) : "memory");
+            }
+        }
+        cp_async_wait_all();
+        __syncwarp();
+        const uint32_t qs = ws_s, ks_ = ws_s + C::MAT_BYTES, vs = ws_s + 2 * C::MAT_BYTES;
+
+        // ---- S = Q K^T ----
+        float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ks++) {
+            uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+            const uint32_t boff = (ks >> 2) * (ROWS * 128);
+            ldsm_x4(qs + boff + sw128((mi & 1) * 8 + (lane & 7), 2 * (ks & 3) + (mi >> 1)), a0, a1, a2, a3);
+            ldsm_x4(ks_ + boff + sw128((mi >> 1) * 8 + (lane & 7), 2 * (ks & 3) + (mi & 1)), b0, b1, b2, b3);
+            mma_bf16_16816(s[0], a0, a1, a2, a3, b0, b1);
+            mma_bf16_16816(s[1], a0, a1, a2, a3, b2, b3);
+        }
+        // ---- masked row softmax (rows r4 and r4 + 8) ----
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int row = r4 + (e >> 1) * 8, key = nt * 8 + c2 + (e & 1);
+                const bool ok = key < seq && (!causal || key <= row);
+                s[nt][e] = ok ? s[nt][e] * sl2 : -INFINITY;
+                mx[e >> 1] = fmaxf(mx[e >> 1], s[nt][e]);
+            }
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            mx[k] = fmaxf(mx[k], __shfl_xor_sync(0xffffffffu, mx[k], 1));
+            mx[k] = fmaxf(mx[k], __shfl_xor_sync(0xffffffffu, mx[k], 2));
+            if (mx[k] == -INFINITY) mx[k] = 0.f;  // padding rows only
+        }
+        float sum[2] = {0.f, 0.f};
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                s[nt][e] = fast_exp2(s[nt][e] - mx[e >> 1]);
+                sum[e >> 1] += s[nt][e];
+            }
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            sum[k] += __shfl_xor_sync(0xffffffffu, sum[k], 1);
+            sum[k] += __shfl_xor_sync(0xffffffffu, sum[k], 2);
+        }
+        // P as the A operand (k = keys): a0 = row r4 keys 0-7, a1 = row r4+8 keys 0-7, a2/a3 keys 8-15; hi + lo parts
+        uint32_t ph[4], pl[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int nt = k >> 1, e = (k & 1) * 2;
+            const float x0 = s[nt][e], x1 = s[nt][e + 1];
+            ph[k] = pack_bf16x2(x0, x1);
+            const float2 hv = unpack_bf16x2(ph[k]);
+            pl[k] = pack_bf16x2(x0 - hv.x, x1 - hv.y);
+        }
+        // ---- O = P V, two d-tiles of 8 per ldmatrix.x4.trans ----
+        const float inv0 = 1.f / sum[0], inv1 = 1.f / sum[1];
+        const int row0 = r4, row1 = r4 + 8;
+        bf16 *o0 = out + (static_cast<long>(n) * seq + row0) * nq * HD + h * HD;
+        bf16 *o1 = out + (static_cast<long>(n) * seq + row1) * nq * HD + h * HD;
+#pragma unroll
+        for (int dt = 0; dt < HD / 8; dt += 2) {
+            uint32_t b0, b1, b2, b3;
+            const int ch = dt + (mi >> 1);
+            ldsm_x4_t(vs + (ch >> 3) * (ROWS * 128) + sw128((mi & 1) * 8 + (lane & 7), ch & 7), b0, b1, b2, b3);
+            float o[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            mma_bf16_16816(o[0], ph[0], ph[1], ph[2], ph[3], b0, b1);
+            mma_bf16_16816(o[0], pl[0], pl[1], pl[2], pl[3], b0, b1);
+            mma_bf16_16816(o[1], ph[0], ph[1], ph[2], ph[3], b2, b3);
+            mma_bf16_16816(o[1], pl[0], pl[1], pl[2], pl[3], b2, b3);
+#pragma unroll
+            for (int t = 0; t < 2; t++) {
+                const int d = (dt + t) * 8 + c2;
+                if (row0 < seq)
+                    *reinterpret_cast<uint32_t *>(o0 + d) = pack_bf16x2(o[t][0] * inv0, o[t][1] * inv0);
+                if (row1 < seq)
+                    *reinterpret_cast<uint32_t *>(o1 + d) = pack_bf16x2(o[t][2] * inv1, o[t][3] * inv1);
+            }
+        }
+        __syncwarp();
+    }
+}
+
+}  // namespace fs

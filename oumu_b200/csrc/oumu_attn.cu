@@ -1,0 +1,358 @@
+// C ABI of the sm_100a attention hot path (declarations and reference citations in include/oumu_attn.h).
+// Host side: argument validation, TMA tensor-map encoding, launch shapes. Nothing here allocates, synchronises
+// or reads device memory (except oumu_device_error), so every entry point can be captured in a CUDA graph.
+#include "../../include/oumu_attn.h"
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "decode.cuh"
+#include "feeders.cuh"
+#include "full_small.cuh"
+#include "prefill_tc.cuh"
+
+namespace {
+
+thread_local char g_last_cuda[256] = "";
+
+int cuda_fail(cudaError_t e) {
+    std::snprintf(g_last_cuda, sizeof(g_last_cuda), "%s", cudaGetErrorString(e));
+    return OUMU_ERR_CUDA;
+}
+#define OUMU_CK(x)                                   \
+    do {                                             \
+        cudaError_t e_ = (x);                        \
+        if (e_ != cudaSuccess) return cuda_fail(e_); \
+    } while (0)
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+constexpr int kMaxDevices = 64;
+constexpr int kSmemMax = 227 * 1024;
+
+struct DevInfo {
+    bool ready = false;
+    int sms = 0;
+};
+DevInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+// SM count of the current device; first use on a device also raises the dynamic shared-memory limit of the
+// kernels that need more than 48 KB.
+int current_device(int *sms) {
+    int d = 0;
+    OUMU_CK(cudaGetDevice(&d));
+    if (d < 0 || d >= kMaxDevices) return OUMU_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    DevInfo &di = g_dev[d];
+    if (!di.ready) {
+        OUMU_CK(cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, d));
+        OUMU_CK(cudaFuncSetAttribute(dec::k_attn_decode<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(dec::k_attn_decode<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(pf::k_attn_prefill<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     pf::Cfg<128>::SMEM));
+        OUMU_CK(cudaFuncSetAttribute(pf::k_attn_prefill<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     pf::Cfg<64>::SMEM));
+        di.ready = true;
+    }
+    *sms = di.sms;
+    return OUMU_OK;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time libcuda dependency).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2-D bf16 map over [outer][inner] (row pitch row_bytes) with a (box_inner x box_outer) box, 128-byte swizzle.
+int make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+             uint32_t box_inner, uint32_t box_outer) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) {
+        std::snprintf(g_last_cuda, sizeof(g_last_cuda), "cuTensorMapEncodeTiled unavailable");
+        return OUMU_ERR_CUDA;
+    }
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        std::snprintf(g_last_cuda, sizeof(g_last_cuda), "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+        return OUMU_ERR_CUDA;
+    }
+    return OUMU_OK;
+}
+
+uint16_t f2b_host(float x) {  // round-to-nearest-even, NaN -> 0x7fc0 (src/gpu.rs:72-78)
+    if (std::isnan(x)) return 0x7fc0;
+    uint32_t u;
+    std::memcpy(&u, &x, 4);
+    return static_cast<uint16_t>((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+}
+float rb_host(float x) {
+    uint32_t u = static_cast<uint32_t>(f2b_host(x)) << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+bool head_dim_ok(int hd) { return hd == 64 || hd == 128; }
+
+size_t decode_counter_bytes(int B, int nk) { return (static_cast<size_t>(B) * nk * 4 + 255) & ~static_cast<size_t>(255); }
+size_t decode_part_bytes(int hd) {
+    return 2 * static_cast<size_t>(hd == 128 ? dec::Cfg<128>::PART_FLOATS : dec::Cfg<64>::PART_FLOATS) * 4;
+}
+
+template <int HD>
+int launch_decode(const void *qkv, const void *kc, const void *vc, void *out, void *ws, size_t ws_bytes,
+                  const int *pos, const int *lens, int B, int nq, int nk, int maxlen, float scale, int sms,
+                  cudaStream_t st) {
+    using C = dec::Cfg<HD>;
+    const long tiles_max = static_cast<long>(B) * nk * ((maxlen + dec::TILE - 1) / dec::TILE);
+    const size_t cbytes = decode_counter_bytes(B, nk), pbytes = decode_part_bytes(HD);
+    if (ws_bytes < cbytes + pbytes) return OUMU_ERR_WORKSPACE;
+    long grid = sms;
+    if (grid > tiles_max) grid = tiles_max;
+    const long fit = static_cast<long>((ws_bytes - cbytes) / pbytes);
+    if (grid > fit) grid = fit;
+    // shared memory: as many 32 KB (hd 128) stages as fit, at most 6
+    dec::Smem<HD> lay{1, B};
+    const int fixed = lay.bytes() - C::STAGE_BYTES + 1024;
+    int stages = (kSmemMax - fixed) / C::STAGE_BYTES;
+    if (stages > 6) stages = 6;
+    if (stages < 2) return OUMU_ERR_UNSUPPORTED;
+    lay.stages = stages;
+    const int smem = lay.bytes() + 1024;
+    CUtensorMap tk, tv;
+    const uint64_t rows = static_cast<uint64_t>(B) * nk * maxlen;
+    int rc = make_map(&tk, kc, HD, rows, HD * 2, 64, dec::TILE);
+    if (rc) return rc;
+    rc = make_map(&tv, vc, HD, rows, HD * 2, 64, dec::TILE);
+    if (rc) return rc;
+    dec::Params P;
+    P.qkv = static_cast<const bf16 *>(qkv);
+    P.out = static_cast<bf16 *>(out);
+    P.cnt = static_cast<int *>(ws);
+    P.part = reinterpret_cast<float *>(static_cast<char *>(ws) + cbytes);
+    P.pos = pos;
+    P.lens = lens;
+    P.B = B;
+    P.nq = nq;
+    P.nk = nk;
+    P.maxlen = maxlen;
+    P.stages = stages;
+    P.sl2 = scale * 1.4426950408889634f;
+    dec::k_attn_decode<HD><<<static_cast<int>(grid), dec::NTHREADS, smem, st>>>(tk, tv, P);
+    OUMU_CK(cudaGetLastError());
+    return OUMU_OK;
+}
+
+template <int HD>
+int launch_small(const void *qkv, void *out, int rows, int seq, int causal, int nq, int nk, float scale, int sms,
+                 cudaStream_t st) {
+    const long units = static_cast<long>(rows / seq) * nq;
+    long grid = (units + fs::WARPS - 1) / fs::WARPS;
+    const long cap = static_cast<long>(sms) * 8;
+    if (grid > cap) grid = cap;
+    const int smem = fs::WARPS * fs::Cfg<HD>::WARP_BYTES;
+    fs::k_attn_small<HD><<<static_cast<int>(grid), fs::WARPS * 32, smem, st>>>(
+        static_cast<const bf16 *>(qkv), static_cast<bf16 *>(out), rows / seq, seq, causal, nq, nk,
+        scale * 1.4426950408889634f);
+    OUMU_CK(cudaGetLastError());
+    return OUMU_OK;
+}
+
+template <int HD>
+int launch_prefill(const void *qkv, void *out, int rows, int seq, int causal, int nq, int nk, float scale,
+                   cudaStream_t st) {
+    CUtensorMap tm;
+    const uint64_t width = static_cast<uint64_t>(nq + 2 * nk) * HD;
+    int rc = make_map(&tm, qkv, width, rows, width * 2, 64, pf::BM);
+    if (rc) return rc;
+    const int nseq = rows / seq;
+    if (nseq > 65535 || nq > 65535) return OUMU_ERR_UNSUPPORTED;
+    dim3 grid((seq + pf::BM - 1) / pf::BM, nq, nseq);
+    pf::k_attn_prefill<HD><<<grid, pf::NTHREADS, pf::Cfg<HD>::SMEM, st>>>(
+        tm, static_cast<bf16 *>(out), seq, causal, nq, nk, scale * 1.4426950408889634f);
+    OUMU_CK(cudaGetLastError());
+    return OUMU_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *oumu_status_string(int s) {
+    switch (s) {
+        case OUMU_OK: return "ok";
+        case OUMU_ERR_INVALID: return "invalid argument";
+        case OUMU_ERR_UNSUPPORTED: return "unsupported shape";
+        case OUMU_ERR_WORKSPACE: return "workspace too small";
+        case OUMU_ERR_CUDA: return "CUDA error";
+        case OUMU_ERR_DEVICE: return "device-side error";
+        default: return "unknown status";
+    }
+}
+
+const char *oumu_last_cuda_error(void) { return g_last_cuda; }
+
+int oumu_rotary_tables(int maxlen, int hd, const double *ext, float *cos_out, float *sin_out) {
+    if (maxlen < 1 || hd < 2 || (hd & 1) || !cos_out || !sin_out) return OUMU_ERR_INVALID;
+    const int half = hd / 2;
+    for (int p = 0; p < maxlen; p++)
+        for (int i = 0; i < half; i++) {
+            const float inv = 1.0f / powf(10000.0f, static_cast<float>(2 * i) / static_cast<float>(hd));
+            const float e = ext ? static_cast<float>(ext[i]) : 1.0f;
+            const float fr = (static_cast<float>(p) * (1.0f / e)) * inv;
+            cos_out[static_cast<long>(p) * half + i] = rb_host(cosf(fr));
+            sin_out[static_cast<long>(p) * half + i] = rb_host(sinf(fr));
+        }
+    return OUMU_OK;
+}
+
+int oumu_rope(void *qkv, const float *cos_t, const float *sin_t, const int *pos, int rows, int seq, int nq, int nk,
+              int hd, oumu_stream_t stream) {
+    if (!qkv || !cos_t || !sin_t || rows < 0 || seq < 0 || nq < 1 || nk < 0) return OUMU_ERR_INVALID;
+    if (seq == 0 && !pos) return OUMU_ERR_INVALID;
+    if (!head_dim_ok(hd)) return OUMU_ERR_UNSUPPORTED;
+    if (!aligned16(qkv) || !aligned16(cos_t) || !aligned16(sin_t)) return OUMU_ERR_INVALID;
+    if (rows == 0) return OUMU_OK;
+    const long total = static_cast<long>(rows) * (nq + nk) * (hd / 16);
+    k_rope<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(static_cast<bf16 *>(qkv), cos_t, sin_t, pos,
+                                                                        rows, seq, nq, nk, hd);
+    OUMU_CK(cudaGetLastError());
+    return OUMU_OK;
+}
+
+int oumu_kv_write(const void *qkv, void *kc, void *vc, const int *pos, int slots, int rows, int nq, int nk, int hd,
+                  int maxlen, oumu_stream_t stream) {
+    if (!qkv || !kc || !vc || slots < 0 || rows < 0 || nq < 0 || nk < 1 || maxlen < 1) return OUMU_ERR_INVALID;
+    if (!head_dim_ok(hd)) return OUMU_ERR_UNSUPPORTED;
+    if (!aligned16(qkv) || !aligned16(kc) || !aligned16(vc)) return OUMU_ERR_INVALID;
+    if (!pos && rows > maxlen) return OUMU_ERR_INVALID;
+    const long total = static_cast<long>(slots) * rows * nk * (hd / 8) * 2;
+    if (total == 0) return OUMU_OK;
+    k_kv_write<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+        static_cast<const bf16 *>(qkv), static_cast<bf16 *>(kc), static_cast<bf16 *>(vc), pos, slots, rows, nq, nk,
+        hd, maxlen);
+    OUMU_CK(cudaGetLastError());
+    return OUMU_OK;
+}
+
+int oumu_decode_prologue(void *qkv, void *kc, void *vc, const float *cos_t, const float *sin_t, const int *pos,
+                         const int *lens, int B, int nq, int nk, int hd, int maxlen, oumu_stream_t stream) {
+    if (!qkv || !kc || !vc || (!pos && !lens) || B < 0 || nq < 1 || nk < 1 || maxlen < 1) return OUMU_ERR_INVALID;
+    if ((cos_t == nullptr) != (sin_t == nullptr)) return OUMU_ERR_INVALID;
+    if (!head_dim_ok(hd)) return OUMU_ERR_UNSUPPORTED;
+    if (!aligned16(qkv) || !aligned16(kc) || !aligned16(vc) || (cos_t && (!aligned16(cos_t) || !aligned16(sin_t))))
+        return OUMU_ERR_INVALID;
+    if (B == 0) return OUMU_OK;
+    k_decode_prologue<<<B, 256, 0, stream>>>(static_cast<bf16 *>(qkv), static_cast<bf16 *>(kc),
+                                             static_cast<bf16 *>(vc), cos_t, sin_t, pos, lens, nq, nk, hd, maxlen);
+    OUMU_CK(cudaGetLastError());
+    return OUMU_OK;
+}
+
+size_t oumu_attn_decode_workspace(int B, int nq, int nk, int hd, int maxlen) {
+    if (B < 1 || nk < 1 || nq % nk || !head_dim_ok(hd) || maxlen < 1) return 0;
+    int sms = 0;
+    if (current_device(&sms) != OUMU_OK) sms = 160;
+    const long tiles_max = static_cast<long>(B) * nk * ((maxlen + dec::TILE - 1) / dec::TILE);
+    const long grid = tiles_max < sms ? tiles_max : sms;
+    return decode_counter_bytes(B, nk) + static_cast<size_t>(grid) * decode_part_bytes(hd);
+}
+
+int oumu_attn_decode_reset(void *workspace, size_t workspace_bytes, int B, int nq, int nk, int hd, int maxlen,
+                           oumu_stream_t stream) {
+    (void)nq;
+    (void)hd;
+    (void)maxlen;
+    if (!workspace || B < 1 || nk < 1) return OUMU_ERR_INVALID;
+    const size_t cb = decode_counter_bytes(B, nk);
+    if (workspace_bytes < cb) return OUMU_ERR_WORKSPACE;
+    OUMU_CK(cudaMemsetAsync(workspace, 0, cb, stream));
+    return OUMU_OK;
+}
+
+int oumu_attn_decode(const void *qkv, const void *kc, const void *vc, void *out, void *workspace,
+                     size_t workspace_bytes, const int *pos, const int *lens, int B, int nq, int nk, int hd,
+                     int maxlen, float scale, oumu_stream_t stream) {
+    if (!qkv || !kc || !vc || !out || !workspace || (!pos && !lens)) return OUMU_ERR_INVALID;
+    if (B < 1 || nq < 1 || nk < 1 || nq % nk || maxlen < 1 || !(scale > 0.f)) return OUMU_ERR_INVALID;
+    if (!head_dim_ok(hd) || nq / nk > dec::GMAX || B > 4096) return OUMU_ERR_UNSUPPORTED;
+    if (static_cast<long>(B) * nk * maxlen >= (1L << 31)) return OUMU_ERR_UNSUPPORTED;
+    if (!aligned16(qkv) || !aligned16(kc) || !aligned16(vc) || !aligned16(out) || !aligned16(workspace))
+        return OUMU_ERR_INVALID;
+    int sms = 0;
+    int rc = current_device(&sms);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (hd == 128)
+        return launch_decode<128>(qkv, kc, vc, out, workspace, workspace_bytes, pos, lens, B, nq, nk, maxlen, scale,
+                                  sms, st);
+    return launch_decode<64>(qkv, kc, vc, out, workspace, workspace_bytes, pos, lens, B, nq, nk, maxlen, scale, sms,
+                             st);
+}
+
+int oumu_attn_full(const void *qkv, void *out, int rows, int seq, int causal, int nq, int nk, int hd, float scale,
+                   oumu_stream_t stream) {
+    if (!qkv || !out || rows < 0 || seq < 1 || nq < 1 || nk < 1 || nq % nk || !(scale > 0.f)) return OUMU_ERR_INVALID;
+    if (rows % seq) return OUMU_ERR_INVALID;
+    if (!head_dim_ok(hd)) return OUMU_ERR_UNSUPPORTED;
+    if (!aligned16(qkv) || !aligned16(out)) return OUMU_ERR_INVALID;
+    if (rows == 0) return OUMU_OK;
+    int sms = 0;
+    int rc = current_device(&sms);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (seq <= fs::ROWS) {
+        return hd == 128 ? launch_small<128>(qkv, out, rows, seq, causal, nq, nk, scale, sms, st)
+                         : launch_small<64>(qkv, out, rows, seq, causal, nq, nk, scale, sms, st);
+    }
+    return hd == 128 ? launch_prefill<128>(qkv, out, rows, seq, causal, nq, nk, scale, st)
+                     : launch_prefill<64>(qkv, out, rows, seq, causal, nq, nk, scale, st);
+}
+
+int oumu_kv_replicate(void *cache, int B, int nk, int maxlen, int hd, int T, oumu_stream_t stream) {
+    if (!cache || B < 1 || nk < 1 || maxlen < 1 || T < 0 || T > maxlen) return OUMU_ERR_INVALID;
+    if (!head_dim_ok(hd)) return OUMU_ERR_UNSUPPORTED;
+    if (!aligned16(cache)) return OUMU_ERR_INVALID;
+    if (B == 1 || T == 0) return OUMU_OK;
+    const int spg = 8;
+    const long total = static_cast<long>(T) * nk * (hd / 8);
+    dim3 grid(static_cast<unsigned>((total + 255) / 256), static_cast<unsigned>((B - 1 + spg - 1) / spg));
+    k_kv_replicate<<<grid, 256, 0, stream>>>(static_cast<bf16 *>(cache), B, nk, maxlen, hd, T, spg);
+    OUMU_CK(cudaGetLastError());
+    return OUMU_OK;
+}
+
+int oumu_device_error(int reset) {
+    unsigned int v = 0;
+    OUMU_CK(cudaMemcpyFromSymbol(&v, oumu_dev_error, sizeof(v)));
+    if (reset) {
+        unsigned int z = 0;
+        OUMU_CK(cudaMemcpyToSymbol(oumu_dev_error, &z, sizeof(z)));
+    }
+    return static_cast<int>(v);
+}
+
+}  // extern "C"

@@ -1,0 +1,267 @@
+// Flash attention on the 5th-generation tensor cores (tcgen05 + TMEM), fed by TMA, for long sequences: the causal
+// prefill over the prompt (src/model.rs:688,701 -> full(..., causal = true)).
+//
+// One CTA per (128-query tile, q head, sequence). Warp roles:
+//   warp 0      TMA producer: Q tile once, then K/V tiles of 128 positions into a 2-stage ring
+//   warp 1      TMEM allocator and the single MMA-issuing thread:
+//                 S  = Q . K_j^T      (M=128 queries, N=128 keys, K=hd; A and B K-major, 128-B swizzle)
+//                 O += P_j . V_j      (M=128, N=hd, K=128 keys; A = P from shared memory, B = V MN-major)
+//   warps 2..5  softmax: thread i owns query row i, reads its S row from TMEM (no cross-thread reduction), keeps
+//               the running max / sum in fp32, writes P_j (bf16) to shared memory, rescales its O row in TMEM
+//               when the max grew, and finally writes bf16(O * (1 / sum)).
+// All waits are bounded (mbar_wait); on a timeout the kernel records the error and winds down.
+#pragma once
+#include "common.cuh"
+
+namespace pf {
+
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int NTHREADS = 6 * 32;
+constexpr int BOX = 128 * 128;  // one 128-row x 128-byte swizzled box
+
+template <int HD>
+struct Cfg {
+    static constexpr int NBOX = HD / 64;
+    static constexpr int Q_OFF = 0;
+    static constexpr int K_OFF = Q_OFF + NBOX * BOX;         // 2 stages
+    static constexpr int V_OFF = K_OFF + 2 * NBOX * BOX;     // 2 stages
+    static constexpr int P_OFF = V_OFF + 2 * NBOX * BOX;     // 2 boxes (keys 0-63, 64-127)
+    static constexpr int BAR_OFF = P_OFF + 2 * BOX;
+    static constexpr int SMEM = BAR_OFF + 128 + 1024;        // + alignment slack
+    static constexpr uint32_t TMEM_COLS = 256;               // S: 128 columns, O: hd columns
+    static constexpr uint32_t O_COL = 128;
+};
+
+// barrier slots (8 bytes each) inside the barrier area
+enum { B_Q = 0, B_KVF0 = 1, B_KVF1 = 2, B_KVE0 = 3, B_KVE1 = 4, B_SFULL = 5, B_SFREE = 6, B_PFULL = 7, B_ODONE = 8,
+       B_TMEM = 12, B_ABORT = 13 };
+
+template <int HD>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    k_attn_prefill(const __grid_constant__ CUtensorMap tqkv, bf16 *__restrict__ out, int seq, int causal, int nq,
+                   int nk, float sl2) {
+    using C = Cfg<HD>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_s = smem_u32(smem_raw);
+    uint8_t *sm = smem_raw + ((1024u - (raw_s & 1023u)) & 1023u);
+    const uint32_t sm_s = smem_u32(sm);
+    const uint32_t bars = sm_s + C::BAR_OFF;
+    auto bar = [&](int i) { return bars + 8u * i; };
+    volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(sm + C::BAR_OFF + 8 * B_TMEM);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + C::BAR_OFF + 8 * B_ABORT);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qt = gridDim.x - 1 - blockIdx.x;  // heaviest causal tiles first
+    const int h = blockIdx.y, n = blockIdx.z, G = nq / nk, kh = h / G;
+    const int q0 = qt * BM;
+    const int row0 = n * seq;  // first row of this sequence in qkv
+    const int ntiles_all = (seq + BN - 1) / BN;
+    const int ntiles = causal ? min(ntiles_all, (q0 + BM - 1) / BN + 1) : ntiles_all;
+
+    if (threadIdx.x == 0) {
+        mbar_init(bar(B_Q), 1);
+        mbar_init(bar(B_KVF0), 1);
+        mbar_init(bar(B_KVF1), 1);
+        mbar_init(bar(B_KVE0), 1);
+        mbar_init(bar(B_KVE1), 1);
+        mbar_init(bar(B_SFULL), 1);
+        mbar_init(bar(B_SFREE), 4);
+        mbar_init(bar(B_PFULL), 4);
+        mbar_init(bar(B_ODONE), 1);
+        *abort_flag = 0;
+        mbar_fence_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(bar(B_TMEM), C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------ TMA producer ------------------------------
+        if (lane == 0) {
+            tma_prefetch_desc(&tqkv);
+            mbar_expect_tx(bar(B_Q), C::NBOX * BOX);
+#pragma unroll
+            for (int bx = 0; bx < C::NBOX; bx++)
+                tma_load_2d(sm_s + C::Q_OFF + bx * BOX, &tqkv, bar(B_Q), h * HD + bx * 64, row0 + q0);
+            for (int j = 0; j < ntiles; j++) {
+                const int st = j & 1;
+                if (j >= 2 && !mbar_wait(bar(B_KVE0 + st), ((j >> 1) - 1) & 1)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                if (*abort_flag) break;
+                const uint32_t fb = bar(B_KVF0 + st);
+                mbar_expect_tx(fb, 2 * C::NBOX * BOX);
+#pragma unroll
+                for (int bx = 0; bx < C::NBOX; bx++) {
+                    tma_load_2d(sm_s + C::K_OFF + (st * C::NBOX + bx) * BOX, &tqkv, fb, (nq + kh) * HD + bx * 64,
+                                row0 + j * BN);
+                    tma_load_2d(sm_s + C::V_OFF + (st * C::NBOX + bx) * BOX, &tqkv, fb,
+                                (nq + nk + kh) * HD + bx * 64, row0 + j * BN);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------ MMA issuer ------------------------------
+        if (lane == 0) {
+            const uint32_t idS = idesc_bf16_f32(BM, BN, 0, 0);
+            const uint32_t idO = idesc_bf16_f32(BM, HD, 0, 1);
+            const uint32_t tS = tmem, tO = tmem + C::O_COL;
+            bool ok = mbar_wait(bar(B_Q), 0);
+            auto issue_S = [&](int j) {
+                const int st = j & 1;
+                const uint32_t kbase = sm_s + C::K_OFF + st * C::NBOX * BOX;
+#pragma unroll
+                for (int ks = 0; ks < HD / 16; ks++) {
+                    const uint64_t a = smem_desc_sw128(sm_s + C::Q_OFF + (ks >> 2) * BOX + (ks & 3) * 32, 16, 1024);
+                    const uint64_t b = smem_desc_sw128(kbase + (ks >> 2) * BOX + (ks & 3) * 32, 16, 1024);
+                    tc_mma_ss(tS, a, b, idS, ks > 0 ? 1u : 0u);
+                }
+                tc_commit(bar(B_SFULL));
+            };
+            if (ok && ntiles > 0) {
+                ok = mbar_wait(bar(B_KVF0), 0);
+                if (ok) {
+                    tc_fence_after();
+                    issue_S(0);
+                }
+            }
+            for (int j = 0; ok && j < ntiles; j++) {
+                if (j + 1 < ntiles) {
+                    // S_{j+1} may overwrite S_j once the softmax warps have read it
+                    ok = mbar_wait(bar(B_KVF0 + ((j + 1) & 1)), ((j + 1) >> 1) & 1) && mbar_wait(bar(B_SFREE), j & 1);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_S(j + 1);
+                }
+                ok = mbar_wait(bar(B_PFULL), j & 1);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t vbase = sm_s + C::V_OFF + (j & 1) * C::NBOX * BOX;
+#pragma unroll
+                for (int kk = 0; kk < BN / 16; kk++) {
+                    const uint64_t a = smem_desc_sw128(sm_s + C::P_OFF + (kk >> 2) * BOX + (kk & 3) * 32, 16, 1024);
+                    const uint64_t b = smem_desc_sw128(vbase + kk * 2048, BOX, 1024);
+                    tc_mma_ss(tO, a, b, idO, (j > 0 || kk > 0) ? 1u : 0u);
+                }
+                tc_commit(bar(B_ODONE));
+                tc_commit(bar(B_KVE0 + (j & 1)));
+            }
+            if (!ok) *abort_flag = 1;
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------ softmax / correction / epilogue ------------------------------
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;  // query row within the tile
+        const int qrow = q0 + r;            // position within the sequence
+        const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+        const uint32_t tS = tmem + lane_off, tO = tmem + lane_off + C::O_COL;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < ntiles && ok; j++) {
+            ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL), j & 1));
+            if (!ok) break;
+            tc_fence_after();
+            uint32_t sr[BN];
+#pragma unroll
+            for (int c = 0; c < BN; c += 32) tmem_ld32(tS + c, sr + c);
+            tc_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_SFREE));
+            // masked, scaled scores and the row max; keys [0, kmax) are visible
+            const int kbase = j * BN;
+            const int kmax = (causal ? min(seq, qrow + 1) : seq) - kbase;
+            float mt = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < BN; c++) {
+                const float v = c < kmax ? __uint_as_float(sr[c]) * sl2 : -INFINITY;
+                sr[c] = __float_as_uint(v);
+                mt = fmaxf(mt, v);
+            }
+            const float mn = fmaxf(m, mt);
+            const float mref = mn == -INFINITY ? 0.f : mn;
+            const float alpha = fast_exp2(m - mref);
+            float rs = 0.f;
+            // P packed to bf16 pairs in place: pair c/2 overwrites a register already consumed
+#pragma unroll
+            for (int c = 0; c < BN; c += 2) {
+                const float p0 = fast_exp2(__uint_as_float(sr[c]) - mref);
+                const float p1 = fast_exp2(__uint_as_float(sr[c + 1]) - mref);
+                rs += p0 + p1;
+                sr[c / 2] = pack_bf16x2(p0, p1);
+            }
+            uint32_t *pk = sr;
+            l = l * alpha + rs;
+            // P_j may overwrite P_{j-1} and O may be rescaled once PV_{j-1} has completed
+            if (j > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE), (j - 1) & 1));
+                if (!ok) break;
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha < 1.f)) {
+#pragma unroll
+                    for (int c = 0; c < HD; c += 32) {
+                        uint32_t orow[32];
+                        tmem_ld32(tO + c, orow);
+                        tc_wait_ld();
+#pragma unroll
+                        for (int k = 0; k < 32; k++) orow[k] = __float_as_uint(__uint_as_float(orow[k]) * alpha);
+                        tmem_st32(tO + c, orow);
+                    }
+                    tc_wait_st();
+                }
+            }
+            m = mn;
+            // P row r -> shared memory, K-major 128-byte swizzle: 16 chunks of 8 keys
+            uint8_t *prow = sm + C::P_OFF;
+#pragma unroll
+            for (int cc = 0; cc < BN / 8; cc++) {
+                uint4 v = make_uint4(pk[cc * 4], pk[cc * 4 + 1], pk[cc * 4 + 2], pk[cc * 4 + 3]);
+                *reinterpret_cast<uint4 *>(prow + (cc >> 3) * BOX + sw128(r, cc & 7)) = v;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_PFULL));
+        }
+        if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE), (ntiles - 1) & 1));
+        if (!ok) *abort_flag = 1;
+        if (ok && ntiles > 0) {
+            tc_fence_after();
+            const float inv = 1.f / l;
+            bf16 *dst = out + static_cast<long>(row0 + qrow) * nq * HD + h * HD;
+#pragma unroll
+            for (int c = 0; c < HD; c += 32) {
+                uint32_t orow[32];
+                tmem_ld32(tO + c, orow);
+                tc_wait_ld();
+                if (qrow < seq) {
+#pragma unroll
+                    for (int k = 0; k < 32; k += 8) {
+                        uint4 v;
+                        v.x = pack_bf16x2(__uint_as_float(orow[k]) * inv, __uint_as_float(orow[k + 1]) * inv);
+                        v.y = pack_bf16x2(__uint_as_float(orow[k + 2]) * inv, __uint_as_float(orow[k + 3]) * inv);
+                        v.z = pack_bf16x2(__uint_as_float(orow[k + 4]) * inv, __uint_as_float(orow[k + 5]) * inv);
+                        v.w = pack_bf16x2(__uint_as_float(orow[k + 6]) * inv, __uint_as_float(orow[k + 7]) * inv);
+                        *reinterpret_cast<uint4 *>(dst + c + k) = v;
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+}  // namespace pf

@@ -1,0 +1,115 @@
+"""Host-side mirror of the reference's attention launch interface, over the C ABI.
+
+Each function has the reference kernel's name and argument meaning (kernels/voxcpm.cu, launched from
+src/model.rs) and takes torch CUDA tensors for the buffers; launches go to the current torch stream, so every call
+can be recorded inside a CUDA graph capture. Errors raise OumuError with the library's status.
+bf16 buffers may be torch.bfloat16 or 16-bit integer tensors holding bf16 bit patterns.
+"""
+import torch
+
+from . import _lib
+
+HD_SUPPORTED = (64, 128)
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def rotary_tables(maxlen, hd, ext=None):
+    """cos, sin fp32 [maxlen][hd/2] built on the host (src/model.rs:337-349), as CPU tensors."""
+    import ctypes
+    import numpy as np
+    cs = np.empty((maxlen, hd // 2), dtype=np.float32)
+    sn = np.empty_like(cs)
+    ext_arr = None if ext is None else np.ascontiguousarray(ext, dtype=np.float64)
+    _lib.call("oumu_rotary_tables", maxlen, hd,
+              None if ext_arr is None else ext_arr.ctypes.data_as(ctypes.c_void_p),
+              cs.ctypes.data_as(ctypes.c_void_p), sn.ctypes.data_as(ctypes.c_void_p))
+    return torch.from_numpy(cs), torch.from_numpy(sn)
+
+
+def rope(qkv, cos_t, sin_t, pos, rows, seq, nq, nk, hd):
+    """In-place rotary embedding (kernels/voxcpm.cu:100-115); pos: int32 device tensor or None when seq > 0."""
+    _lib.call("oumu_rope", _p(qkv), _p(cos_t), _p(sin_t), _p(pos), rows, seq, nq, nk, hd, _stream())
+
+
+def kv_write(qkv, kc, vc, pos, slots, rows, nq, nk, hd, maxlen):
+    """k/v of `rows` positions of every slot into the caches at *pos (or 0) (kernels/voxcpm.cu:117-129)."""
+    _lib.call("oumu_kv_write", _p(qkv), _p(kc), _p(vc), _p(pos), slots, rows, nq, nk, hd, maxlen, _stream())
+
+
+def decode_prologue(qkv, kc, vc, cos_t, sin_t, pos, lens, B, nq, nk, hd, maxlen):
+    """rope + kv_write of one decode position per take, one launch (src/model.rs:580-595)."""
+    _lib.call("oumu_decode_prologue", _p(qkv), _p(kc), _p(vc), _p(cos_t), _p(sin_t), _p(pos), _p(lens), B, nq, nk,
+              hd, maxlen, _stream())
+
+
+def decode_workspace_bytes(B, nq, nk, hd, maxlen):
+    return int(_lib.load().oumu_attn_decode_workspace(B, nq, nk, hd, maxlen))
+
+
+def decode_workspace(B, nq, nk, hd, maxlen, device=None):
+    """A zero-filled workspace for attn_decode (counters start at zero; every call leaves them at zero)."""
+    n = decode_workspace_bytes(B, nq, nk, hd, maxlen)
+    if n == 0:
+        raise ValueError("unsupported decode shape")
+    return torch.zeros(n, dtype=torch.uint8, device=device or "cuda")
+
+
+def reference_part_bytes(B, nq, hd, maxlen, att_ch=64):
+    """Size of the reference's StepBufs::att_part (src/model.rs:237)."""
+    return 4 * B * nq * (maxlen // att_ch) * (hd + 2)
+
+
+def attn_decode(qkv, kc, vc, out, workspace, pos, lens, B, nq, nk, hd, maxlen, scale):
+    """Split-KV decode attention with the combine fused (replaces attn_decode + attn_combine,
+    kernels/voxcpm.cu:131-185). Lengths: lens[s] (int32 device tensor) or *pos + 1."""
+    _lib.call("oumu_attn_decode", _p(qkv), _p(kc), _p(vc), _p(out), _p(workspace), workspace.numel(), _p(pos),
+              _p(lens), B, nq, nk, hd, maxlen, float(scale), _stream())
+
+
+def attn_decode_reset(workspace, B, nq, nk, hd, maxlen):
+    _lib.call("oumu_attn_decode_reset", _p(workspace), workspace.numel(), B, nq, nk, hd, maxlen, _stream())
+
+
+def attn_full(qkv, out, rows, seq, causal, nq, nk, hd, scale):
+    """Attention inside independent sequences of length seq (kernels/voxcpm.cu:262-297)."""
+    _lib.call("oumu_attn_full", _p(qkv), _p(out), rows, seq, int(bool(causal)), nq, nk, hd, float(scale), _stream())
+
+
+def kv_replicate(c, B, nk, maxlen, hd, T):
+    """Slot 0 -> slots 1..B-1 for positions < T (kernels/voxcpm.cu:407-413)."""
+    _lib.call("oumu_kv_replicate", _p(c), B, nk, maxlen, hd, T, _stream())
+
+
+def device_error(reset=False):
+    """The library's device-side error word on the current device (synchronises)."""
+    return int(_lib.load().oumu_device_error(1 if reset else 0))
+
+
+# ------------------------------------------------------------------------------------------------------------
+# The attention launch sequences of Engine (src/model.rs), per layer
+# ------------------------------------------------------------------------------------------------------------
+
+def step_tf_attention(qkv, kc, vc, att, workspace, cos_t, sin_t, ctr, lens, B, nq, nk, hd, maxlen, rope_on=True):
+    """One decode position of one layer for every take, as Engine::step_tf does (src/model.rs:578-615):
+    rope + kv_write (one prologue launch) then decode attention with the combine fused (one launch)."""
+    decode_prologue(qkv, kc, vc, cos_t if rope_on else None, sin_t if rope_on else None, ctr, lens, B, nq, nk, hd,
+                    maxlen)
+    attn_decode(qkv, kc, vc, att, workspace, ctr if lens is None else None, lens, B, nq, nk, hd, maxlen,
+                1.0 / hd ** 0.5)
+
+
+def full_attention(qkv, att, rows, seq, causal, nq, nk, hd, maxlen=0, cos_t=None, sin_t=None, kc=None, vc=None):
+    """The attention part of one layer of Engine::full (src/model.rs:541-567): rope over positions r % seq,
+    kv_write of every row into slot 0 when caches are given, then attention inside the sequences."""
+    if cos_t is not None:
+        rope(qkv, cos_t, sin_t, None, rows, seq, nq, nk, hd)
+    if kc is not None:
+        kv_write(qkv, kc, vc, None, 1, rows, nq, nk, hd, maxlen)
+    attn_full(qkv, att, rows, seq, causal, nq, nk, hd, 1.0 / hd ** 0.5)

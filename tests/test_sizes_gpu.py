@@ -1,0 +1,219 @@
+"""The kernels at the benchmark configurations' full sizes and at the edges the reference handles: per-take lengths
+1 .. maxlen, maxlen 65536, ragged prefill lengths, the reference-sized workspace, CUDA-graph replay with positions
+read on the device, determinism, and the device error word."""
+import numpy as np
+import pytest
+import torch
+
+import golden_cases as gc
+from oumu_b200 import ops, synth
+from oracle import cpu
+
+pytestmark = pytest.mark.gpu
+
+NQ, NK, HD = 16, 2, 128
+
+
+def rand_bf16(shape, seed, device="cuda"):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    return torch.randn(shape, generator=g, device=device, dtype=torch.float32).to(torch.bfloat16)
+
+
+def u16(t):
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def decode_case(B, lens, maxlen, nq=NQ, nk=NK, hd=HD, seed=0):
+    qkv = rand_bf16((B, (nq + 2 * nk) * hd), seed)
+    kc = rand_bf16((B, nk, maxlen, hd), seed + 1)
+    vc = rand_bf16((B, nk, maxlen, hd), seed + 2)
+    ln = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    return qkv, kc, vc, ln
+
+
+def run_decode(qkv, kc, vc, ln, B, maxlen, nq=NQ, nk=NK, hd=HD, ws=None):
+    att = torch.zeros((B, nq * hd), dtype=torch.bfloat16, device="cuda")
+    ws = ops.decode_workspace(B, nq, nk, hd, maxlen) if ws is None else ws
+    ops.attn_decode(qkv, kc, vc, att, ws, None, ln, B, nq, nk, hd, maxlen, hd ** -0.5)
+    torch.cuda.synchronize()
+    return att, ws
+
+
+def oracle_decode(qkv, kc, vc, lens, B, maxlen, nq=NQ, nk=NK, hd=HD):
+    return cpu.attn_decode(u16(qkv), u16(kc), u16(vc), None, np.asarray(lens, np.int32), B, nq, nk, hd, maxlen,
+                           hd ** -0.5)
+
+
+def test_decode_config2_layer_vs_oracle(cuda):
+    # BASELINE config 2, one layer: 64 takes, slots of 4096, lengths uniform in [330, 4096]
+    B, maxlen = 64, 4096
+    lens = synth.uniform_int(synth.config_seed(1), B, 330, 4096)
+    qkv, kc, vc, ln = decode_case(B, lens, maxlen, seed=10)
+    att, ws = run_decode(qkv, kc, vc, ln, B, maxlen)
+    gc.assert_close(u16(att), oracle_decode(qkv, kc, vc, lens, B, maxlen), "config 2 layer")
+    # the combine counters are left at zero, and a second call is bit-identical
+    cnt = ws[: B * NK * 4].view(torch.int32)
+    assert int(cnt.abs().sum()) == 0
+    att2, _ = run_decode(qkv, kc, vc, ln, B, maxlen, ws=ws)
+    assert torch.equal(att.view(torch.int16), att2.view(torch.int16))
+
+
+@pytest.mark.parametrize("nq,nk,hd", [(16, 2, 128), (16, 2, 64), (8, 8, 128), (12, 4, 64), (7, 1, 128)])
+def test_decode_shapes_and_lengths(cuda, nq, nk, hd):
+    maxlen = 640
+    lens = [1, 2, 63, 64, 65, 127, 128, 129, 333, 639, 640]
+    B = len(lens)
+    qkv, kc, vc, ln = decode_case(B, lens, maxlen, nq, nk, hd, seed=20)
+    att, _ = run_decode(qkv, kc, vc, ln, B, maxlen, nq, nk, hd)
+    gc.assert_close(u16(att), oracle_decode(qkv, kc, vc, lens, B, maxlen, nq, nk, hd), f"{nq}/{nk}/{hd}")
+
+
+def test_decode_shared_position_and_max_length(cuda):
+    # the reference's form: one shared *pos for every take; and the longest KV the reference accepts (65536)
+    B, maxlen = 2, 65536
+    qkv, kc, vc, _ = decode_case(B, [maxlen] * B, maxlen, seed=30)
+    att = torch.zeros((B, NQ * HD), dtype=torch.bfloat16, device="cuda")
+    ws = ops.decode_workspace(B, NQ, NK, HD, maxlen)
+    pos = torch.tensor([maxlen - 1], dtype=torch.int32, device="cuda")
+    ops.attn_decode(qkv, kc, vc, att, ws, pos, None, B, NQ, NK, HD, maxlen, HD ** -0.5)
+    torch.cuda.synchronize()
+    gc.assert_close(u16(att), oracle_decode(qkv, kc, vc, [maxlen] * B, B, maxlen), "maxlen 65536")
+
+
+def test_decode_reference_sized_workspace(cuda):
+    # config 1 (one take, 512 of 4096) with exactly the reference's att_part bytes (src/model.rs:237)
+    B, maxlen, lens = 1, 4096, [512]
+    qkv, kc, vc, ln = decode_case(B, lens, maxlen, seed=40)
+    nbytes = ops.reference_part_bytes(B, NQ, HD, maxlen)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    att, _ = run_decode(qkv, kc, vc, ln, B, maxlen, ws=ws)
+    gc.assert_close(u16(att), oracle_decode(qkv, kc, vc, lens, B, maxlen), "reference-sized workspace")
+    small = torch.zeros(1024, dtype=torch.uint8, device="cuda")
+    with pytest.raises(Exception) as e:
+        run_decode(qkv, kc, vc, ln, B, maxlen, ws=small)
+    assert "workspace" in str(e.value)
+
+
+def test_decode_graph_replay_matches_eager(cuda):
+    # Engine::decode captures one step and replays it, positions advancing on the device (src/model.rs:777-796)
+    layers, B, maxlen, start = 3, 8, 512, 200
+    W = (NQ + 2 * NK) * HD
+    cs, sn = ops.rotary_tables(maxlen, HD)
+    cs, sn = cs.cuda(), sn.cuda()
+
+    def make_state():
+        torch.manual_seed(0)
+        st = dict(qkv=[rand_bf16((B, W), 50 + l) for l in range(layers)],
+                  kc=[rand_bf16((B, NK, maxlen, HD), 60 + l) for l in range(layers)],
+                  vc=[rand_bf16((B, NK, maxlen, HD), 70 + l) for l in range(layers)],
+                  att=[torch.zeros((B, NQ * HD), dtype=torch.bfloat16, device="cuda") for _ in range(layers)],
+                  ctr=torch.tensor([start, 0, 0, 0], dtype=torch.int32, device="cuda"),
+                  ws=ops.decode_workspace(B, NQ, NK, HD, maxlen))
+        return st
+
+    def step(st):
+        for l in range(layers):
+            ops.step_tf_attention(st["qkv"][l], st["kc"][l], st["vc"][l], st["att"][l], st["ws"], cs, sn,
+                                  st["ctr"], None, B, NQ, NK, HD, maxlen)
+        st["ctr"][0:1].add_(1)
+
+    eager = make_state()
+    graphed = make_state()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            step(graphed)
+    torch.cuda.current_stream().wait_stream(s)
+    # capture records without running: the graphed state is still the initial one
+    for _ in range(5):
+        step(eager)
+        g.replay()
+    torch.cuda.synchronize()
+    assert int(graphed["ctr"][0]) == start + 5 == int(eager["ctr"][0])
+    for l in range(layers):
+        assert torch.equal(eager["att"][l].view(torch.int16), graphed["att"][l].view(torch.int16))
+        assert torch.equal(eager["kc"][l].view(torch.int16), graphed["kc"][l].view(torch.int16))
+    # and the last step against the oracle
+    l = layers - 1
+    L = start + 5
+    ref = oracle_decode(graphed["qkv"][l], graphed["kc"][l], graphed["vc"][l], [L] * B, B, maxlen)
+    gc.assert_close(u16(graphed["att"][l]), ref, "graph replay")
+    del g
+
+
+def test_decode_prologue_equals_rope_then_kv_write(cuda):
+    B, maxlen = 6, 256
+    W = (NQ + 2 * NK) * HD
+    cs, sn = ops.rotary_tables(maxlen, HD)
+    cs, sn = cs.cuda(), sn.cuda()
+    lens = torch.tensor([1, 5, 64, 100, 255, 256], dtype=torch.int32, device="cuda")
+    q0 = rand_bf16((B, W), 80)
+    a = dict(q=q0.clone(), k=torch.zeros((B, NK, maxlen, HD), dtype=torch.bfloat16, device="cuda"))
+    a["v"] = torch.zeros_like(a["k"])
+    b = {k: v.clone() for k, v in a.items()}
+    ops.decode_prologue(a["q"], a["k"], a["v"], cs, sn, None, lens, B, NQ, NK, HD, maxlen)
+    for s in range(B):  # the reference's pair, one take at a time at its own position
+        p = torch.tensor([int(lens[s]) - 1], dtype=torch.int32, device="cuda")
+        ops.rope(b["q"][s:s + 1], cs, sn, p, 1, 0, NQ, NK, HD)
+        ops.kv_write(b["q"][s:s + 1], b["k"][s:s + 1], b["v"][s:s + 1], p, 1, 1, NQ, NK, HD, maxlen)
+    torch.cuda.synchronize()
+    for key in a:
+        assert torch.equal(a[key].view(torch.int16), b[key].view(torch.int16)), key
+    # without tables (residual LM, no rope): q untouched, k/v copied
+    c = dict(q=q0.clone(), k=torch.zeros_like(a["k"]), v=torch.zeros_like(a["v"]))
+    ops.decode_prologue(c["q"], c["k"], c["v"], None, None, None, lens, B, NQ, NK, HD, maxlen)
+    torch.cuda.synchronize()
+    assert torch.equal(c["q"].view(torch.int16), q0.view(torch.int16))
+    row = q0.view(B, NQ + 2 * NK, HD)
+    for s in range(B):
+        assert torch.equal(c["k"][s, :, int(lens[s]) - 1], row[s, NQ:NQ + NK])
+
+
+@pytest.mark.parametrize("T,causal,hd,nq,nk", [(1024, 1, 128, 16, 2), (1000, 1, 128, 16, 2), (129, 1, 128, 16, 2),
+                                               (17, 1, 128, 16, 2), (300, 0, 64, 8, 2), (256, 0, 128, 4, 4)])
+def test_prefill_vs_oracle(cuda, T, causal, hd, nq, nk):
+    W = (nq + 2 * nk) * hd
+    qkv = rand_bf16((T, W), 90 + T)
+    out = torch.zeros((T, nq * hd), dtype=torch.bfloat16, device="cuda")
+    ops.attn_full(qkv, out, T, T, causal, nq, nk, hd, hd ** -0.5)
+    torch.cuda.synchronize()
+    ref = cpu.attn_full(u16(qkv), T, T, causal, nq, nk, hd, hd ** -0.5)
+    gc.assert_close(u16(out), ref, f"prefill T={T}")
+
+
+@pytest.mark.parametrize("nseq,seq,nq,nk,hd", [(512, 12, 16, 16, 64), (512, 11, 16, 2, 128), (256, 5, 16, 2, 128)])
+def test_locdit_full_size_vs_oracle(cuda, nseq, seq, nq, nk, hd):
+    # config 4 (256 takes x 2 CFG = 512 sequences of 12 tokens, 16 heads, hd 64) and the reference's DiT / LocEnc
+    rows, W = nseq * seq, (nq + 2 * nk) * hd
+    qkv = rand_bf16((rows, W), 100 + seq)
+    out = torch.zeros((rows, nq * hd), dtype=torch.bfloat16, device="cuda")
+    ops.attn_full(qkv, out, rows, seq, 0, nq, nk, hd, hd ** -0.5)
+    torch.cuda.synchronize()
+    gc.assert_close(u16(out), cpu.attn_full(u16(qkv), rows, seq, 0, nq, nk, hd, hd ** -0.5), f"seq {seq}")
+
+
+def test_kv_replicate_config3(cuda):
+    # config 3: the prompt KV (T = 1024) copied into 64 take slots of 4096 positions
+    B, maxlen, T = 64, 4096, 1024
+    c = torch.zeros((B, NK, maxlen, HD), dtype=torch.bfloat16, device="cuda")
+    c[0, :, :T] = rand_bf16((NK, T, HD), 110)
+    c[1:, :, T:T + 8] = 1.0  # positions >= T must stay untouched
+    ops.kv_replicate(c, B, NK, maxlen, HD, T)
+    torch.cuda.synchronize()
+    assert torch.equal(c[1:, :, :T].view(torch.int16), c[:1, :, :T].expand(B - 1, -1, -1, -1).view(torch.int16))
+    assert bool((c[1:, :, T:T + 8] == 1.0).all())
+
+
+def test_device_error_word(cuda):
+    assert ops.device_error() == 0
+    # a length outside [1, maxlen] is clamped by the kernel and recorded (no out-of-range access)
+    B, maxlen = 2, 128
+    qkv, kc, vc, _ = decode_case(B, [1, 1], maxlen, seed=120)
+    ln = torch.tensor([0, maxlen + 5], dtype=torch.int32, device="cuda")
+    att, ws = run_decode(qkv, kc, vc, ln, B, maxlen)
+    assert bool(torch.isfinite(att.float()).all())
+    assert ops.device_error(reset=True) & 2
+    assert ops.device_error() == 0
