@@ -41,6 +41,18 @@ const char *oumu_status_string(int status);
 const char *oumu_last_cuda_error(void);
 
 /*
+ * Programmatic dependent launch for the decode kernels (oumu_decode_prologue, oumu_attn_decode,
+ * oumu_attn_decode_step), process-wide,
+ * off by default; returns the previous setting. When on, these kernels are launched so that they may start while
+ * the preceding kernel in the stream is still running: their set-up, and the loads of cache positions below each
+ * take's newest position, overlap it; q, the newest position and every global write wait for it to complete. The
+ * caller guarantees that the preceding kernels of the same step do not write `pos`/`lens` or cache positions below
+ * the newest one (true of the reference's step, where ctr advances only in step_end, src/model.rs:771, and
+ * kv_write writes only position *pos, src/model.rs:590-595). Captured into CUDA graphs as programmatic edges.
+ */
+int oumu_set_pdl(int enable);
+
+/*
  * Rotary tables, host side. Replaces rotary_tables (src/model.rs:337-349): for position p < maxlen and
  * i < hd/2, fr = (p * (1 / ext[i])) * (1 / 10000^(2i/hd)) in fp32, cos/sin rounded to bf16 and stored as fp32.
  * ext == NULL means ext[i] = 1 (plain base-10000 RoPE). cos_out/sin_out are HOST arrays of maxlen*hd/2 floats.
@@ -99,6 +111,20 @@ int oumu_attn_decode_reset(void *workspace, size_t workspace_bytes, int B, int n
 int oumu_attn_decode(const void *qkv, const void *kc, const void *vc, void *out, void *workspace,
                      size_t workspace_bytes, const int *pos, const int *lens, int B, int nq, int nk, int hd,
                      int maxlen, float scale, oumu_stream_t stream);
+
+/*
+ * One decode layer in one launch: the decode prologue and the decode attention of oumu_decode_prologue +
+ * oumu_attn_decode fused. For every take s at position p_s (lens[s] - 1, or *pos): its k at p_s is rotated
+ * (cos_t/sin_t; NULL for no rope) and written with v into cache slot s, its q is rotated in registers, and the
+ * attention over positions <= p_s is written to `out`, bit-identical to the two separate calls. Buffer effects
+ * differ only in qkv: the rotated k is written back into qkv as rope does, the q heads are left unrotated (the
+ * reference reads qkv no further after attention, src/model.rs:622-632).
+ * Replaces the rope + kv_write + attn_decode + attn_combine sequence of Engine::step_tf (src/model.rs:580-615).
+ * Same workspace as oumu_attn_decode.
+ */
+int oumu_attn_decode_step(void *qkv, void *kc, void *vc, void *out, void *workspace, size_t workspace_bytes,
+                          const float *cos_t, const float *sin_t, const int *pos, const int *lens, int B, int nq,
+                          int nk, int hd, int maxlen, float scale, oumu_stream_t stream);
 
 /*
  * Attention inside independent sequences of length `seq` held in a fused qkv buffer of `rows` = nseq * seq rows;

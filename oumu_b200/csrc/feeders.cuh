@@ -77,6 +77,8 @@ __global__ void __launch_bounds__(256) k_decode_prologue(bf16 *qkv, bf16 *kc, bf
                                                          const float *sin_t, const int *pos, const int *lens, int nq,
                                                          int nk, int hd, int maxlen) {
     const int s = blockIdx.x, half = hd / 2, groups = half / 8;
+    if (threadIdx.x == 0) pdl_trigger();
+    pdl_wait();
     int p = lens ? lens[s] - 1 : *pos;
     if (p < 0 || p >= maxlen) {
         if (threadIdx.x == 0) record_error(OUMU_DEVERR_LENGTH);

@@ -3,10 +3,12 @@
 // or reads device memory (except oumu_device_error), so every entry point can be captured in a CUDA graph.
 #include "../../include/oumu_attn.h"
 
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "common.cuh"
 #include "decode.cuh"
@@ -30,6 +32,24 @@ int cuda_fail(cudaError_t e) {
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+std::atomic<int> g_pdl{0};
+
+// Launch with programmatic stream serialization when oumu_set_pdl(1) is in effect.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = g_pdl.load(std::memory_order_relaxed) ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 constexpr int kMaxDevices = 64;
 constexpr int kSmemMax = 227 * 1024;
 
@@ -50,8 +70,14 @@ int current_device(int *sms) {
     DevInfo &di = g_dev[d];
     if (!di.ready) {
         OUMU_CK(cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, d));
-        OUMU_CK(cudaFuncSetAttribute(dec::k_attn_decode<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax));
-        OUMU_CK(cudaFuncSetAttribute(dec::k_attn_decode<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(dec::k_attn_decode<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(dec::k_attn_decode<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(dec::k_attn_decode<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(dec::k_attn_decode<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
         OUMU_CK(cudaFuncSetAttribute(pf::k_attn_prefill<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      pf::Cfg<128>::SMEM));
         OUMU_CK(cudaFuncSetAttribute(pf::k_attn_prefill<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -122,10 +148,10 @@ size_t decode_part_bytes(int hd) {
     return 2 * static_cast<size_t>(hd == 128 ? dec::Cfg<128>::PART_FLOATS : dec::Cfg<64>::PART_FLOATS) * 4;
 }
 
-template <int HD>
+template <int HD, bool FUSED>
 int launch_decode(const void *qkv, const void *kc, const void *vc, void *out, void *ws, size_t ws_bytes,
-                  const int *pos, const int *lens, int B, int nq, int nk, int maxlen, float scale, int sms,
-                  cudaStream_t st) {
+                  const int *pos, const int *lens, const float *cos_t, const float *sin_t, int B, int nq, int nk,
+                  int maxlen, float scale, int sms, cudaStream_t st) {
     using C = dec::Cfg<HD>;
     const long tiles_max = static_cast<long>(B) * nk * ((maxlen + dec::TILE - 1) / dec::TILE);
     const size_t cbytes = decode_counter_bytes(B, nk), pbytes = decode_part_bytes(HD);
@@ -134,13 +160,9 @@ int launch_decode(const void *qkv, const void *kc, const void *vc, void *out, vo
     if (grid > tiles_max) grid = tiles_max;
     const long fit = static_cast<long>((ws_bytes - cbytes) / pbytes);
     if (grid > fit) grid = fit;
-    // shared memory: as many 32 KB (hd 128) stages as fit, at most 6
-    dec::Smem<HD> lay{1, B};
-    const int fixed = lay.bytes() - C::STAGE_BYTES + 1024;
-    int stages = (kSmemMax - fixed) / C::STAGE_BYTES;
-    if (stages > 6) stages = 6;
-    if (stages < 2) return OUMU_ERR_UNSUPPORTED;
-    lay.stages = stages;
+    // shared memory: one stage per consumer warp, plus 1 KB to align the base to 1024 B
+    const dec::Smem<HD> lay{B};
+    if (lay.bytes() + 1024 > kSmemMax) return OUMU_ERR_UNSUPPORTED;
     const int smem = lay.bytes() + 1024;
     CUtensorMap tk, tv;
     const uint64_t rows = static_cast<uint64_t>(B) * nk * maxlen;
@@ -149,7 +171,11 @@ int launch_decode(const void *qkv, const void *kc, const void *vc, void *out, vo
     rc = make_map(&tv, vc, HD, rows, HD * 2, 64, dec::TILE);
     if (rc) return rc;
     dec::Params P;
-    P.qkv = static_cast<const bf16 *>(qkv);
+    P.qkv = static_cast<bf16 *>(const_cast<void *>(qkv));
+    P.kc = static_cast<bf16 *>(const_cast<void *>(kc));
+    P.vc = static_cast<bf16 *>(const_cast<void *>(vc));
+    P.cos_t = cos_t;
+    P.sin_t = sin_t;
     P.out = static_cast<bf16 *>(out);
     P.cnt = static_cast<int *>(ws);
     P.part = reinterpret_cast<float *>(static_cast<char *>(ws) + cbytes);
@@ -159,10 +185,9 @@ int launch_decode(const void *qkv, const void *kc, const void *vc, void *out, vo
     P.nq = nq;
     P.nk = nk;
     P.maxlen = maxlen;
-    P.stages = stages;
     P.sl2 = scale * 1.4426950408889634f;
-    dec::k_attn_decode<HD><<<static_cast<int>(grid), dec::NTHREADS, smem, st>>>(tk, tv, P);
-    OUMU_CK(cudaGetLastError());
+    OUMU_CK(launch_k(dec::k_attn_decode<HD, FUSED>, dim3(static_cast<unsigned>(grid)), dim3(dec::NTHREADS), smem, st,
+                     tk, tv, P));
     return OUMU_OK;
 }
 
@@ -215,6 +240,8 @@ const char *oumu_status_string(int s) {
 
 const char *oumu_last_cuda_error(void) { return g_last_cuda; }
 
+int oumu_set_pdl(int enable) { return g_pdl.exchange(enable ? 1 : 0); }
+
 int oumu_rotary_tables(int maxlen, int hd, const double *ext, float *cos_out, float *sin_out) {
     if (maxlen < 1 || hd < 2 || (hd & 1) || !cos_out || !sin_out) return OUMU_ERR_INVALID;
     const int half = hd / 2;
@@ -266,9 +293,9 @@ int oumu_decode_prologue(void *qkv, void *kc, void *vc, const float *cos_t, cons
     if (!aligned16(qkv) || !aligned16(kc) || !aligned16(vc) || (cos_t && (!aligned16(cos_t) || !aligned16(sin_t))))
         return OUMU_ERR_INVALID;
     if (B == 0) return OUMU_OK;
-    k_decode_prologue<<<B, 256, 0, stream>>>(static_cast<bf16 *>(qkv), static_cast<bf16 *>(kc),
-                                             static_cast<bf16 *>(vc), cos_t, sin_t, pos, lens, nq, nk, hd, maxlen);
-    OUMU_CK(cudaGetLastError());
+    OUMU_CK(launch_k(k_decode_prologue, dim3(B), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream),
+                     static_cast<bf16 *>(qkv), static_cast<bf16 *>(kc), static_cast<bf16 *>(vc), cos_t, sin_t, pos,
+                     lens, nq, nk, hd, maxlen));
     return OUMU_OK;
 }
 
@@ -293,24 +320,46 @@ int oumu_attn_decode_reset(void *workspace, size_t workspace_bytes, int B, int n
     return OUMU_OK;
 }
 
-int oumu_attn_decode(const void *qkv, const void *kc, const void *vc, void *out, void *workspace,
-                     size_t workspace_bytes, const int *pos, const int *lens, int B, int nq, int nk, int hd,
-                     int maxlen, float scale, oumu_stream_t stream) {
+namespace {
+int decode_entry(bool fused, const void *qkv, const void *kc, const void *vc, void *out, void *workspace,
+                 size_t workspace_bytes, const float *cos_t, const float *sin_t, const int *pos, const int *lens, int B,
+                 int nq, int nk, int hd, int maxlen, float scale, oumu_stream_t stream) {
     if (!qkv || !kc || !vc || !out || !workspace || (!pos && !lens)) return OUMU_ERR_INVALID;
     if (B < 1 || nq < 1 || nk < 1 || nq % nk || maxlen < 1 || !(scale > 0.f)) return OUMU_ERR_INVALID;
+    if ((cos_t == nullptr) != (sin_t == nullptr)) return OUMU_ERR_INVALID;
     if (!head_dim_ok(hd) || nq / nk > dec::GMAX || B > 4096) return OUMU_ERR_UNSUPPORTED;
     if (static_cast<long>(B) * nk * maxlen >= (1L << 31)) return OUMU_ERR_UNSUPPORTED;
-    if (!aligned16(qkv) || !aligned16(kc) || !aligned16(vc) || !aligned16(out) || !aligned16(workspace))
+    if (!aligned16(qkv) || !aligned16(kc) || !aligned16(vc) || !aligned16(out) || !aligned16(workspace) ||
+        (cos_t && (!aligned16(cos_t) || !aligned16(sin_t))))
         return OUMU_ERR_INVALID;
     int sms = 0;
     int rc = current_device(&sms);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (hd == 128)
-        return launch_decode<128>(qkv, kc, vc, out, workspace, workspace_bytes, pos, lens, B, nq, nk, maxlen, scale,
-                                  sms, st);
-    return launch_decode<64>(qkv, kc, vc, out, workspace, workspace_bytes, pos, lens, B, nq, nk, maxlen, scale, sms,
-                             st);
+    if (fused)
+        return hd == 128 ? launch_decode<128, true>(qkv, kc, vc, out, workspace, workspace_bytes, pos, lens, cos_t,
+                                                    sin_t, B, nq, nk, maxlen, scale, sms, st)
+                         : launch_decode<64, true>(qkv, kc, vc, out, workspace, workspace_bytes, pos, lens, cos_t,
+                                                   sin_t, B, nq, nk, maxlen, scale, sms, st);
+    return hd == 128 ? launch_decode<128, false>(qkv, kc, vc, out, workspace, workspace_bytes, pos, lens, nullptr,
+                                                 nullptr, B, nq, nk, maxlen, scale, sms, st)
+                     : launch_decode<64, false>(qkv, kc, vc, out, workspace, workspace_bytes, pos, lens, nullptr,
+                                                nullptr, B, nq, nk, maxlen, scale, sms, st);
+}
+}  // namespace
+
+int oumu_attn_decode(const void *qkv, const void *kc, const void *vc, void *out, void *workspace,
+                     size_t workspace_bytes, const int *pos, const int *lens, int B, int nq, int nk, int hd,
+                     int maxlen, float scale, oumu_stream_t stream) {
+    return decode_entry(false, qkv, kc, vc, out, workspace, workspace_bytes, nullptr, nullptr, pos, lens, B, nq, nk,
+                        hd, maxlen, scale, stream);
+}
+
+int oumu_attn_decode_step(void *qkv, void *kc, void *vc, void *out, void *workspace, size_t workspace_bytes,
+                          const float *cos_t, const float *sin_t, const int *pos, const int *lens, int B, int nq,
+                          int nk, int hd, int maxlen, float scale, oumu_stream_t stream) {
+    return decode_entry(true, qkv, kc, vc, out, workspace, workspace_bytes, cos_t, sin_t, pos, lens, B, nq, nk, hd,
+                        maxlen, scale, stream);
 }
 
 int oumu_attn_full(const void *qkv, void *out, int rows, int seq, int causal, int nq, int nk, int hd, float scale,

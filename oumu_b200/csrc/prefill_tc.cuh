@@ -7,8 +7,9 @@
 //                 S  = Q . K_j^T      (M=128 queries, N=128 keys, K=hd; A and B K-major, 128-B swizzle)
 //                 O += P_j . V_j      (M=128, N=hd, K=128 keys; A = P from shared memory, B = V MN-major)
 //   warps 2..5  softmax: thread i owns query row i, reads its S row from TMEM (no cross-thread reduction), keeps
-//               the running max / sum in fp32, writes P_j (bf16) to shared memory, rescales its O row in TMEM
-//               when the max grew, and finally writes bf16(O * (1 / sum)).
+//               the running max / sum in fp32, writes P_j to shared memory as two bf16 matrices hi + lo (so the
+//               weights keep ~16 mantissa bits; O += P_hi.V + P_lo.V), rescales its O row in TMEM when the max
+//               grew, and finally writes bf16(O * (1 / sum)).
 // All waits are bounded (mbar_wait); on a timeout the kernel records the error and winds down.
 #pragma once
 #include "common.cuh"
@@ -26,8 +27,9 @@ struct Cfg {
     static constexpr int Q_OFF = 0;
     static constexpr int K_OFF = Q_OFF + NBOX * BOX;         // 2 stages
     static constexpr int V_OFF = K_OFF + 2 * NBOX * BOX;     // 2 stages
-    static constexpr int P_OFF = V_OFF + 2 * NBOX * BOX;     // 2 boxes (keys 0-63, 64-127)
-    static constexpr int BAR_OFF = P_OFF + 2 * BOX;
+    static constexpr int P_OFF = V_OFF + 2 * NBOX * BOX;     // P hi: 2 boxes (keys 0-63, 64-127), then P lo
+    static constexpr int PLO_OFF = P_OFF + 2 * BOX;
+    static constexpr int BAR_OFF = PLO_OFF + 2 * BOX;
     static constexpr int SMEM = BAR_OFF + 128 + 1024;        // + alignment slack
     static constexpr uint32_t TMEM_COLS = 256;               // S: 128 columns, O: hd columns
     static constexpr uint32_t O_COL = 128;
@@ -146,9 +148,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const uint32_t vbase = sm_s + C::V_OFF + (j & 1) * C::NBOX * BOX;
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; kk++) {
-                    const uint64_t a = smem_desc_sw128(sm_s + C::P_OFF + (kk >> 2) * BOX + (kk & 3) * 32, 16, 1024);
+                    const uint32_t poff = (kk >> 2) * BOX + (kk & 3) * 32;
                     const uint64_t b = smem_desc_sw128(vbase + kk * 2048, BOX, 1024);
-                    tc_mma_ss(tO, a, b, idO, (j > 0 || kk > 0) ? 1u : 0u);
+                    tc_mma_ss(tO, smem_desc_sw128(sm_s + C::P_OFF + poff, 16, 1024), b, idO, (j > 0 || kk > 0) ? 1u : 0u);
+                    tc_mma_ss(tO, smem_desc_sw128(sm_s + C::PLO_OFF + poff, 16, 1024), b, idO, 1u);
                 }
                 tc_commit(bar(B_ODONE));
                 tc_commit(bar(B_KVE0 + (j & 1)));
@@ -179,26 +182,30 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             // masked, scaled scores and the row max; keys [0, kmax) are visible
             const int kbase = j * BN;
             const int kmax = (causal ? min(seq, qrow + 1) : seq) - kbase;
-            float mt = -INFINITY;
+            float mt8[8];
 #pragma unroll
-            for (int c = 0; c < BN; c++) {
+            for (int k = 0; k < 8; k++) mt8[k] = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < BN; c++) {  // eight independent max chains
                 const float v = c < kmax ? __uint_as_float(sr[c]) * sl2 : -INFINITY;
                 sr[c] = __float_as_uint(v);
-                mt = fmaxf(mt, v);
+                mt8[c & 7] = fmaxf(mt8[c & 7], v);
             }
+            const float mt = fmaxf(fmaxf(fmaxf(mt8[0], mt8[1]), fmaxf(mt8[2], mt8[3])),
+                                   fmaxf(fmaxf(mt8[4], mt8[5]), fmaxf(mt8[6], mt8[7])));
             const float mn = fmaxf(m, mt);
             const float mref = mn == -INFINITY ? 0.f : mn;
             const float alpha = fast_exp2(m - mref);
-            float rs = 0.f;
-            // P packed to bf16 pairs in place: pair c/2 overwrites a register already consumed
+            float rs8[8];
 #pragma unroll
-            for (int c = 0; c < BN; c += 2) {
-                const float p0 = fast_exp2(__uint_as_float(sr[c]) - mref);
-                const float p1 = fast_exp2(__uint_as_float(sr[c + 1]) - mref);
-                rs += p0 + p1;
-                sr[c / 2] = pack_bf16x2(p0, p1);
+            for (int k = 0; k < 8; k++) rs8[k] = 0.f;
+#pragma unroll
+            for (int c = 0; c < BN; c++) {  // eight independent sum chains
+                const float p = fast_exp2(__uint_as_float(sr[c]) - mref);
+                rs8[c & 7] += p;
+                sr[c] = __float_as_uint(p);
             }
-            uint32_t *pk = sr;
+            const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
             l = l * alpha + rs;
             // P_j may overwrite P_{j-1} and O may be rescaled once PV_{j-1} has completed
             if (j > 0) {
@@ -219,12 +226,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
             }
             m = mn;
-            // P row r -> shared memory, K-major 128-byte swizzle: 16 chunks of 8 keys
-            uint8_t *prow = sm + C::P_OFF;
+            // P row r -> shared memory, K-major 128-byte swizzle: 16 chunks of 8 keys, hi and lo parts
 #pragma unroll
             for (int cc = 0; cc < BN / 8; cc++) {
-                uint4 v = make_uint4(pk[cc * 4], pk[cc * 4 + 1], pk[cc * 4 + 2], pk[cc * 4 + 3]);
-                *reinterpret_cast<uint4 *>(prow + (cc >> 3) * BOX + sw128(r, cc & 7)) = v;
+                uint32_t hi[4], lo[4];
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const float p0 = __uint_as_float(sr[cc * 8 + 2 * k]), p1 = __uint_as_float(sr[cc * 8 + 2 * k + 1]);
+                    hi[k] = pack_bf16x2(p0, p1);
+                    const float2 h = unpack_bf16x2(hi[k]);
+                    lo[k] = pack_bf16x2(p0 - h.x, p1 - h.y);
+                }
+                const uint32_t off = (cc >> 3) * BOX + sw128(r, cc & 7);
+                *reinterpret_cast<uint4 *>(sm + C::P_OFF + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<uint4 *>(sm + C::PLO_OFF + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             tc_fence_before();

@@ -73,6 +73,13 @@ def attn_decode(qkv, kc, vc, out, workspace, pos, lens, B, nq, nk, hd, maxlen, s
               _p(lens), B, nq, nk, hd, maxlen, float(scale), _stream())
 
 
+def attn_decode_step(qkv, kc, vc, out, workspace, cos_t, sin_t, pos, lens, B, nq, nk, hd, maxlen, scale):
+    """One decode layer in one launch: rope + kv_write of the newest position fused into the split-KV attention
+    (replaces rope + kv_write + attn_decode + attn_combine of Engine::step_tf, src/model.rs:580-615)."""
+    _lib.call("oumu_attn_decode_step", _p(qkv), _p(kc), _p(vc), _p(out), _p(workspace), workspace.numel(),
+              _p(cos_t), _p(sin_t), _p(pos), _p(lens), B, nq, nk, hd, maxlen, float(scale), _stream())
+
+
 def attn_decode_reset(workspace, B, nq, nk, hd, maxlen):
     _lib.call("oumu_attn_decode_reset", _p(workspace), workspace.numel(), B, nq, nk, hd, maxlen, _stream())
 
@@ -87,6 +94,11 @@ def kv_replicate(c, B, nk, maxlen, hd, T):
     _lib.call("oumu_kv_replicate", _p(c), B, nk, maxlen, hd, T, _stream())
 
 
+def set_pdl(enable):
+    """Programmatic dependent launch for the decode kernels (see oumu_set_pdl); returns the previous setting."""
+    return bool(_lib.load().oumu_set_pdl(1 if enable else 0))
+
+
 def device_error(reset=False):
     """The library's device-side error word on the current device (synchronises)."""
     return int(_lib.load().oumu_device_error(1 if reset else 0))
@@ -96,13 +108,18 @@ def device_error(reset=False):
 # The attention launch sequences of Engine (src/model.rs), per layer
 # ------------------------------------------------------------------------------------------------------------
 
-def step_tf_attention(qkv, kc, vc, att, workspace, cos_t, sin_t, ctr, lens, B, nq, nk, hd, maxlen, rope_on=True):
-    """One decode position of one layer for every take, as Engine::step_tf does (src/model.rs:578-615):
-    rope + kv_write (one prologue launch) then decode attention with the combine fused (one launch)."""
-    decode_prologue(qkv, kc, vc, cos_t if rope_on else None, sin_t if rope_on else None, ctr, lens, B, nq, nk, hd,
-                    maxlen)
-    attn_decode(qkv, kc, vc, att, workspace, ctr if lens is None else None, lens, B, nq, nk, hd, maxlen,
-                1.0 / hd ** 0.5)
+def step_tf_attention(qkv, kc, vc, att, workspace, cos_t, sin_t, ctr, lens, B, nq, nk, hd, maxlen, rope_on=True,
+                      fused=True):
+    """One decode position of one layer for every take, as Engine::step_tf does (src/model.rs:578-615): one fused
+    launch (rope + kv_write + split-KV attention with the combine), or with fused=False the prologue launch then
+    the attention launch."""
+    cs, sn = (cos_t, sin_t) if rope_on else (None, None)
+    pos = ctr if lens is None else None
+    if fused:
+        attn_decode_step(qkv, kc, vc, att, workspace, cs, sn, pos, lens, B, nq, nk, hd, maxlen, 1.0 / hd ** 0.5)
+        return
+    decode_prologue(qkv, kc, vc, cs, sn, ctr, lens, B, nq, nk, hd, maxlen)
+    attn_decode(qkv, kc, vc, att, workspace, pos, lens, B, nq, nk, hd, maxlen, 1.0 / hd ** 0.5)
 
 
 def full_attention(qkv, att, rows, seq, causal, nq, nk, hd, maxlen=0, cos_t=None, sin_t=None, kc=None, vc=None):

@@ -139,6 +139,7 @@ def _host(t):
 def run_gpu(c, impl, x=None):
     import torch
     x = inputs(c) if x is None else x
+    fused = impl == "ours_fused"
     if impl == "ref":
         from oracle import refkern as K
     else:
@@ -187,11 +188,22 @@ def run_gpu(c, impl, x=None):
         qkv = torch.zeros((B, width(c)), dtype=torch.int16, device="cuda")
         for s, (L, pr) in enumerate(zip(lens, x["prompts"])):
             q = _dev(pr)
+            if fused:
+                # positions < L-1 as a prefill would leave them; the newest row goes through the fused decode step
+                if L > 1:
+                    K.rope(q, cs, sn, None, L - 1, L, nq, nk, hd)
+                    K.kv_write(q, kc[s:s + 1], vc[s:s + 1], None, 1, L - 1, nq, nk, hd, maxlen)
+                qkv[s] = q[L - 1]
+                continue
             K.rope(q, cs, sn, None, L, L, nq, nk, hd)
             K.kv_write(q, kc[s:s + 1], vc[s:s + 1], None, 1, L, nq, nk, hd, maxlen)
             qkv[s] = q[L - 1]
         att = torch.zeros((B, nq * hd), dtype=torch.int16, device="cuda")
-        if impl == "ref":
+        if fused:
+            ws = K.decode_workspace(B, nq, nk, hd, maxlen)
+            ln = torch.tensor(lens, dtype=torch.int32, device="cuda")
+            K.attn_decode_step(qkv, kc, vc, att, ws, cs, sn, None, ln, B, nq, nk, hd, maxlen, scale(c))
+        elif impl == "ref":
             part = torch.zeros(B * nq * (maxlen // 64) * (hd + 2), dtype=torch.float32, device="cuda")
             K.attn_decode_per_take(qkv, kc, vc, part, att, lens, B, nq, nk, hd, maxlen, scale(c))
         else:

@@ -51,3 +51,19 @@ def test_ours_matches_reference_kernels_live(cuda, name):
     c = gc.CASES[name]
     x = gc.inputs(c)
     _check(c["kind"], gc.run_gpu(c, "ours", x), gc.run_gpu(c, "ref", x), name)
+
+
+DECODE = [n for n in NAMES if gc.CASES[n]["kind"] == "decode"]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", DECODE)
+def test_fused_decode_step_matches_golden_and_unfused(cuda, name):
+    # the newest position goes through the fused launch (rope + kv_write + attention): the same output as the
+    # separate launches, bit for bit, and the reference's output within tolerance
+    c = gc.CASES[name]
+    x = gc.inputs(c)
+    fused = gc.run_gpu(c, "ours_fused", x)
+    gc.assert_exact(fused["out"], gc.run_gpu(c, "ours", x)["out"], name)
+    path = os.path.join(GOLDEN, name + ".npz")
+    gc.assert_close(fused["out"], np.load(path)["out"], name)

@@ -59,6 +59,22 @@ def test_decode_config2_layer_vs_oracle(cuda):
     assert torch.equal(att.view(torch.int16), att2.view(torch.int16))
 
 
+def test_decode_config2_layers_back_to_back(cuda):
+    # several layers launched back to back on one workspace, as in a step: every output checked
+    B, maxlen, layers = 64, 4096, 4
+    lens = synth.uniform_int(synth.config_seed(1), B, 330, 4096)
+    data = [decode_case(B, lens, maxlen, seed=200 + 10 * l) for l in range(layers)]
+    ws = ops.decode_workspace(B, NQ, NK, HD, maxlen)
+    outs = [torch.zeros((B, NQ * HD), dtype=torch.bfloat16, device="cuda") for _ in range(layers)]
+    for _ in range(3):
+        for l, (qkv, kc, vc, ln) in enumerate(data):
+            ops.attn_decode(qkv, kc, vc, outs[l], ws, None, ln, B, NQ, NK, HD, maxlen, HD ** -0.5)
+    torch.cuda.synchronize()
+    for l, (qkv, kc, vc, _) in enumerate(data):
+        gc.assert_close(u16(outs[l]), oracle_decode(qkv, kc, vc, lens, B, maxlen), f"layer {l}")
+    assert int(ws[: B * NK * 4].view(torch.int32).abs().sum()) == 0
+
+
 @pytest.mark.parametrize("nq,nk,hd", [(16, 2, 128), (16, 2, 64), (8, 8, 128), (12, 4, 64), (7, 1, 128)])
 def test_decode_shapes_and_lengths(cuda, nq, nk, hd):
     maxlen = 640
@@ -95,7 +111,8 @@ def test_decode_reference_sized_workspace(cuda):
     assert "workspace" in str(e.value)
 
 
-def test_decode_graph_replay_matches_eager(cuda):
+@pytest.mark.parametrize("pdl,fused", [(False, False), (True, False), (False, True), (True, True)])
+def test_decode_graph_replay_matches_eager(cuda, pdl, fused):
     # Engine::decode captures one step and replays it, positions advancing on the device (src/model.rs:777-796)
     layers, B, maxlen, start = 3, 8, 512, 200
     W = (NQ + 2 * NK) * HD
@@ -115,7 +132,7 @@ def test_decode_graph_replay_matches_eager(cuda):
     def step(st):
         for l in range(layers):
             ops.step_tf_attention(st["qkv"][l], st["kc"][l], st["vc"][l], st["att"][l], st["ws"], cs, sn,
-                                  st["ctr"], None, B, NQ, NK, HD, maxlen)
+                                  st["ctr"], None, B, NQ, NK, HD, maxlen, fused=fused)
         st["ctr"][0:1].add_(1)
 
     eager = make_state()
@@ -123,9 +140,13 @@ def test_decode_graph_replay_matches_eager(cuda):
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(s):
-        with torch.cuda.graph(g, stream=s):
-            step(graphed)
+    prev = ops.set_pdl(pdl)  # programmatic edges inside the captured step only
+    try:
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                step(graphed)
+    finally:
+        ops.set_pdl(prev)
     torch.cuda.current_stream().wait_stream(s)
     # capture records without running: the graphed state is still the initial one
     for _ in range(5):
@@ -136,12 +157,40 @@ def test_decode_graph_replay_matches_eager(cuda):
     for l in range(layers):
         assert torch.equal(eager["att"][l].view(torch.int16), graphed["att"][l].view(torch.int16))
         assert torch.equal(eager["kc"][l].view(torch.int16), graphed["kc"][l].view(torch.int16))
-    # and the last step against the oracle
+    # and the last step against the oracle (the caches hold the rotated keys of every written position)
     l = layers - 1
     L = start + 5
-    ref = oracle_decode(graphed["qkv"][l], graphed["kc"][l], graphed["vc"][l], [L] * B, B, maxlen)
+    q = graphed["qkv"][l].clone()
+    if fused:  # the fused launch leaves q unrotated in qkv: rotate it the reference's way for the oracle
+        ops.rope(q, cs, sn, graphed["ctr"][0:1] - 1, B, 0, NQ, NK, HD)
+        torch.cuda.synchronize()
+    ref = oracle_decode(q, graphed["kc"][l], graphed["vc"][l], [L] * B, B, maxlen)
     gc.assert_close(u16(graphed["att"][l]), ref, "graph replay")
     del g
+
+
+@pytest.mark.parametrize("rope_on", [True, False])
+def test_fused_step_equals_prologue_then_attention(cuda, rope_on):
+    # config 2 shape: outputs, caches and the k part of qkv bit-identical; q left unrotated by the fused launch
+    B, maxlen = 64, 4096
+    lens = synth.uniform_int(synth.config_seed(1), B, 330, 4096)
+    cs, sn = ops.rotary_tables(maxlen, HD)
+    cs, sn = (cs.cuda(), sn.cuda()) if rope_on else (None, None)
+    qkv, kc, vc, ln = decode_case(B, lens, maxlen, seed=300)
+    a = dict(q=qkv.clone(), k=kc.clone(), v=vc.clone(), o=torch.zeros((B, NQ * HD), dtype=torch.bfloat16,
+                                                                        device="cuda"))
+    b = {k: v.clone() for k, v in a.items()}
+    ws = ops.decode_workspace(B, NQ, NK, HD, maxlen)
+    ops.step_tf_attention(a["q"], a["k"], a["v"], a["o"], ws, cs, sn, None, ln, B, NQ, NK, HD, maxlen,
+                          rope_on=rope_on, fused=False)
+    ops.step_tf_attention(b["q"], b["k"], b["v"], b["o"], ws, cs, sn, None, ln, B, NQ, NK, HD, maxlen,
+                          rope_on=rope_on, fused=True)
+    torch.cuda.synchronize()
+    for key in ("o", "k", "v"):
+        assert torch.equal(a[key].view(torch.int16), b[key].view(torch.int16)), key
+    W = NQ * HD
+    assert torch.equal(a["q"][:, W:].view(torch.int16), b["q"][:, W:].view(torch.int16))
+    assert torch.equal(b["q"][:, :W].view(torch.int16), qkv[:, :W].view(torch.int16))
 
 
 def test_decode_prologue_equals_rope_then_kv_write(cuda):
