@@ -113,6 +113,24 @@ int oumu_attn_decode(const void *qkv, const void *kc, const void *vc, void *out,
                      int maxlen, float scale, oumu_stream_t stream);
 
 /*
+ * Decode attention that allocates nothing and takes no workspace: oumu_attn_decode with its scratch (split-KV
+ * partials and combine counters) in a static device array of OUMU_DECODE_STATIC_SCRATCH_BYTES that the library
+ * holds on every device that loads it, until the process exits. For callers that cannot give the library device
+ * memory: a plug-in that sees only its input and output buffers, or a graph capture where allocating is not an
+ * option. No counterpart in the reference (its att_part is allocated by the engine, src/model.rs:237).
+ * The array holds one counter per (take, kv head) and at least one CTA's partials; shapes with more than about
+ * 522,000 takes x kv heads do not fit and are rejected with OUMU_ERR_WORKSPACE and a message in
+ * oumu_last_cuda_error (with fewer than one CTA per SM's worth of room the kernel runs on fewer CTAs). The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress); make that first call before any stream capture. Every call clears the counters
+ * (an asynchronous memset on `stream`) and then uses the shared array, so calls that can overlap on the GPU (other
+ * streams, other host threads) race with each other: serialise them.
+ */
+#define OUMU_DECODE_STATIC_SCRATCH_BYTES (2 * 1024 * 1024)
+int oumu_attn_decode_static(const void *qkv, const void *kc, const void *vc, void *out, const int *pos,
+                            const int *lens, int B, int nq, int nk, int hd, int maxlen, float scale,
+                            oumu_stream_t stream);
+
+/*
  * One decode layer in one launch: the decode prologue and the decode attention of oumu_decode_prologue +
  * oumu_attn_decode fused. For every take s at position p_s (lens[s] - 1, or *pos): its k at p_s is rotated
  * (cos_t/sin_t; NULL for no rope) and written with v into cache slot s, its q is rotated in registers, and the

@@ -26,6 +26,7 @@ SIGNATURES = {
     "oumu_attn_decode_workspace": (_Z, [_I, _I, _I, _I, _I]),
     "oumu_attn_decode_reset": (_I, [_P, _Z, _I, _I, _I, _I, _I, _P]),
     "oumu_attn_decode": (_I, [_P, _P, _P, _P, _P, _Z, _P, _P, _I, _I, _I, _I, _I, _F, _P]),
+    "oumu_attn_decode_static": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P]),
     "oumu_attn_decode_step": (_I, [_P, _P, _P, _P, _P, _Z, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P]),
     "oumu_attn_full": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _F, _P]),
     "oumu_kv_replicate": (_I, [_P, _I, _I, _I, _I, _I, _P]),

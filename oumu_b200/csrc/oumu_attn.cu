@@ -355,6 +355,63 @@ int oumu_attn_decode(const void *qkv, const void *kc, const void *vc, void *out,
                         hd, maxlen, scale, stream);
 }
 
+}  // extern "C"
+
+// ------------------------------------------------------------------------------------------------------------
+// Decode attention without a caller-supplied workspace.
+//
+// Some hosts cannot hand this library device memory for scratch: a plug-in that receives only its input and output
+// buffers from an engine that owns every device allocation, or a caller recording into a CUDA graph where a
+// cudaMalloc would break the capture and the per-call workspace was never planned for. For them the split-KV
+// partials and the combine counters live in this file-scope array instead: every device that loads the library
+// keeps its own copy, OUMU_DECODE_STATIC_SCRATCH_BYTES large, until the process exits.
+// ------------------------------------------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char oumu_decode_static_scratch[OUMU_DECODE_STATIC_SCRATCH_BYTES];
+
+namespace {
+void *g_static_scratch[kMaxDevices] = {};
+std::mutex g_static_mu;
+
+// Device address of the static scratch on the current device. In host code the array's name only stands for the
+// device symbol, so its address is looked up once per device (with that device current) and kept.
+int static_scratch_ptr(void **out) {
+    int d = 0;
+    OUMU_CK(cudaGetDevice(&d));
+    if (d < 0 || d >= kMaxDevices) return OUMU_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_static_scratch[d]) {
+        void *p = nullptr;
+        OUMU_CK(cudaGetSymbolAddress(&p, oumu_decode_static_scratch));
+        g_static_scratch[d] = p;
+    }
+    *out = g_static_scratch[d];
+    return OUMU_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int oumu_attn_decode_static(const void *qkv, const void *kc, const void *vc, void *out, const int *pos,
+                            const int *lens, int B, int nq, int nk, int hd, int maxlen, float scale,
+                            oumu_stream_t stream) {
+    if (B < 1 || nk < 1 || nq < 1 || nq % nk || !head_dim_ok(hd)) return OUMU_ERR_INVALID;
+    // the scratch this shape needs: the combine counters, then one partial pair per CTA (at least one CTA)
+    const size_t cbytes = decode_counter_bytes(B, nk);
+    if (cbytes + decode_part_bytes(hd) > OUMU_DECODE_STATIC_SCRATCH_BYTES) {
+        std::snprintf(g_last_cuda, sizeof(g_last_cuda),
+                      "oumu_attn_decode_static: B * nk = %d needs %zu bytes of scratch, the static scratch holds %d",
+                      B * nk, cbytes + decode_part_bytes(hd), OUMU_DECODE_STATIC_SCRATCH_BYTES);
+        return OUMU_ERR_WORKSPACE;
+    }
+    void *ws = nullptr;
+    int rc = static_scratch_ptr(&ws);
+    if (rc) return rc;
+    // the counters must start at zero; the array keeps whatever the previous call (or an aborted one) left
+    OUMU_CK(cudaMemsetAsync(ws, 0, cbytes, reinterpret_cast<cudaStream_t>(stream)));
+    return decode_entry(false, qkv, kc, vc, out, ws, OUMU_DECODE_STATIC_SCRATCH_BYTES, nullptr, nullptr, pos, lens,
+                        B, nq, nk, hd, maxlen, scale, stream);
+}
+
 int oumu_attn_decode_step(void *qkv, void *kc, void *vc, void *out, void *workspace, size_t workspace_bytes,
                           const float *cos_t, const float *sin_t, const int *pos, const int *lens, int B, int nq,
                           int nk, int hd, int maxlen, float scale, oumu_stream_t stream) {
