@@ -44,6 +44,17 @@ def bytes_per_layer(lens):
     return int(sum(2 * NK * int(L) * HD * 2 + 2 * NQ * HD * 2 for L in lens))
 
 
+def rank_reduce(x, op, dist=None, device="cpu"):
+    """x reduced over the ranks of the default process group (op "max" for device times, "sum" for bytes);
+    x itself without a group. Every rank must call it at the same point."""
+    if dist is None or not dist.is_initialized() or dist.get_world_size() == 1:
+        return x
+    import torch
+    t = torch.tensor([float(x)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 def measured_peak():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -273,18 +284,10 @@ def main():
         torch.cuda.synchronize()
 
     def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return rank_reduce(x, "max", dist if world > 1 else None, dev)
 
     def sum_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
+        return rank_reduce(x, "sum", dist if world > 1 else None, dev)
 
     # ---- device-resident timing ----
     t_end = time.perf_counter() + 0.3

@@ -1,0 +1,54 @@
+"""The multi-GPU plumbing of bench.py on CPU ranks (gloo, world size 2): each rank owns its own takes (disjoint,
+seeded per rank, no collective on the data path) and rank 0 reports the summed bytes over the max device time."""
+import os
+import sys
+from datetime import timedelta
+
+import pytest
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _worker(rank, world, port, q):
+    import torch.distributed as dist
+    sys.path.insert(0, ROOT)
+    import bench
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    try:
+        lens = bench.take_lengths(rank)
+        per_step = bench.LAYERS * bench.bytes_per_layer(lens)
+        ms = 10.0 + 3.0 * rank  # each rank's own (pretend) device time
+        total = bench.rank_reduce(per_step, "sum", dist)
+        slowest = bench.rank_reduce(ms, "max", dist)
+        q.put((rank, [int(x) for x in lens], per_step, total, slowest))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_ranks_shard_takes_and_aggregate():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + (os.getpid() % 1000)
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r = q.get(timeout=120)
+        res[r[0]] = r
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    (_, l0, b0, t0, m0), (_, l1, b1, t1, m1) = res[0], res[1]
+    assert len(l0) == len(l1) == 64 and l0 != l1             # each rank its own 64 takes
+    assert all(330 <= x <= 4096 for x in l0 + l1)
+    assert t0 == t1 == b0 + b1                               # bytes of all ranks
+    assert m0 == m1 == 13.0                                  # the slowest rank's time
+
+
+def test_single_process_reduce_is_identity():
+    sys.path.insert(0, ROOT)
+    import bench
+    assert bench.rank_reduce(5.0, "max") == 5.0
