@@ -44,6 +44,7 @@ constexpr int GMAX = 8;      // q heads per kv head handled by one mma column bl
 // from the phase before.)
 constexpr int STAGES = 2 * NCW;
 constexpr int NFB = 1;       // flush buffer between the consumers and the merger
+constexpr int MIN_TILES = 4; // tiles per CTA at least: small problems use fewer CTAs rather than many 1-tile partials
 
 template <int HD>
 struct Cfg {
@@ -223,6 +224,7 @@ __device__ __forceinline__ void merge_segment(const Params &P, const float *F, i
 #pragma unroll
         for (int e = 0; e < DL; e++) o[k][e] = 0.f;
     }
+#pragma unroll 4
     for (int cc = cf; cc <= cl; cc++) {
         const long ac = static_cast<long>(cc) * W / Gc;
         const float *rc = P.part + (static_cast<long>(cc) * 2 + ((cc == cf && ac < Sg) ? 1 : 0)) * C::PART_FLOATS;
@@ -230,6 +232,7 @@ __device__ __forceinline__ void merge_segment(const Params &P, const float *F, i
         for (int k = 0; k < NH; k++)
             if (hb + k * HS < GMAX) M2[k] = fmaxf(M2[k], __ldcg(rc + hb + k * HS));
     }
+#pragma unroll 2
     for (int cc = cf; cc <= cl; cc++) {
         const long ac = static_cast<long>(cc) * W / Gc;
         const float *rc = P.part + (static_cast<long>(cc) * 2 + ((cc == cf && ac < Sg) ? 1 : 0)) * C::PART_FLOATS;
@@ -408,10 +411,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     __syncthreads();
 
-    // Effective grid: never more CTAs than tiles, so every CTA range [c*W/Gc, (c+1)*W/Gc) is non-empty and every
-    // CTA between the first and the last of a segment contributes a partial to it.
+    // Effective grid: at most one CTA per MIN_TILES tiles, so every CTA range [c*W/Gc, (c+1)*W/Gc) is non-empty and
+    // every CTA between the first and the last of a segment contributes a partial to it.
     const long W = pre[B];
-    const int Gc = static_cast<int>(W < static_cast<long>(gridDim.x) ? W : static_cast<long>(gridDim.x));
+    const long want = (W + MIN_TILES - 1) / MIN_TILES;
+    const int Gc = static_cast<int>(want < static_cast<long>(gridDim.x) ? want : static_cast<long>(gridDim.x));
     const int c = blockIdx.x;
     if (threadIdx.x == 0) pdl_trigger();
     if (c >= Gc) return;

@@ -6,10 +6,14 @@
 //   warp 1      TMEM allocator and the single MMA-issuing thread:
 //                 S  = Q . K_j^T      (M=128 queries, N=128 keys, K=hd; A and B K-major, 128-B swizzle)
 //                 O += P_j . V_j      (M=128, N=hd, K=128 keys; A = P from shared memory, B = V MN-major)
-//   warps 2..5  softmax: thread i owns query row i, reads its S row from TMEM (no cross-thread reduction), keeps
-//               the running max / sum in fp32, writes P_j to shared memory as two bf16 matrices hi + lo (so the
-//               weights keep ~16 mantissa bits; O += P_hi.V + P_lo.V), rescales its O row in TMEM when the max
-//               grew, and finally writes bf16(O * (1 / sum)).
+//   warps 2..9  softmax, two warpgroups: warpgroup g owns columns [64g, 64g+64) of every row (thread = row of its
+//               TMEM lane quarter). Each thread reads its whole S row from TMEM for the row max (the two halves of a
+//               row compute the same value, so nothing is exchanged), exponentiates its own 64 columns, keeps its
+//               half of the row sum, writes its half of P_j to shared memory as two bf16 matrices hi + lo (so the
+//               weights keep ~16 mantissa bits; O += P_hi.V + P_lo.V) and rescales its half of the O row in TMEM
+//               when the max has grown by more than 2^8 (lazy rescaling: until then the stale max is kept, which
+//               changes no result because O and the sum use the same one). The halves of the sum meet once, at the
+//               end, and each warpgroup writes bf16(O * (1 / sum)) for its 64 columns.
 // All waits are bounded (mbar_wait); on a timeout the kernel records the error and winds down.
 #pragma once
 #include "common.cuh"
@@ -18,7 +22,8 @@ namespace pf {
 
 constexpr int BM = 128;
 constexpr int BN = 128;
-constexpr int NTHREADS = 6 * 32;
+constexpr int NTHREADS = 10 * 32;  // TMA, MMA, two softmax warpgroups
+constexpr float RESCALE_LOG2 = 8.f;  // O and the sum are rescaled only when the row max grows by more than 2^8
 constexpr int BOX = 128 * 128;  // one 128-row x 128-byte swizzled box
 
 template <int HD>
@@ -68,8 +73,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         mbar_init(bar(B_KVE0), 1);
         mbar_init(bar(B_KVE1), 1);
         mbar_init(bar(B_SFULL), 1);
-        mbar_init(bar(B_SFREE), 4);
-        mbar_init(bar(B_PFULL), 4);
+        mbar_init(bar(B_SFREE), 8);
+        mbar_init(bar(B_PFULL), 8);
         mbar_init(bar(B_ODONE), 1);
         *abort_flag = 0;
         mbar_fence_init();
@@ -161,47 +166,66 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         __syncwarp();
     } else {
         // ------------------------------ softmax / correction / epilogue ------------------------------
-        const int quarter = warp & 3;
+        const int quarter = warp & 3, wg = (warp - 2) >> 2;
         const int r = quarter * 32 + lane;  // query row within the tile
         const int qrow = q0 + r;            // position within the sequence
+        const int cb = wg * 64;             // this warpgroup's columns [cb, cb + 64)
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
         const uint32_t tS = tmem + lane_off, tO = tmem + lane_off + C::O_COL;
-        float m = -INFINITY, l = 0.f;
+        constexpr int OH = HD / 2;          // O columns per warpgroup
+        float m = -INFINITY, l = 0.f;       // max in log2 units of the scaled score; this thread's half of the sum
         bool ok = true;
         for (int j = 0; j < ntiles && ok; j++) {
             ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL), j & 1));
             if (!ok) break;
             tc_fence_after();
-            uint32_t sr[BN];
-#pragma unroll
-            for (int c = 0; c < BN; c += 32) tmem_ld32(tS + c, sr + c);
-            tc_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(B_SFREE));
-            // masked, scaled scores and the row max; keys [0, kmax) are visible
+            // keys [0, kmax) are visible; only the causal diagonal tile and a ragged last tile need the mask
             const int kbase = j * BN;
+            const bool masked = (causal && kbase + BN - 1 > q0) || kbase + BN > seq;
             const int kmax = (causal ? min(seq, qrow + 1) : seq) - kbase;
+            // the row max over all 128 columns (both warpgroups compute the same value)
             float mt8[8];
 #pragma unroll
             for (int k = 0; k < 8; k++) mt8[k] = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < BN; c++) {  // eight independent max chains
-                const float v = c < kmax ? __uint_as_float(sr[c]) * sl2 : -INFINITY;
-                sr[c] = __float_as_uint(v);
-                mt8[c & 7] = fmaxf(mt8[c & 7], v);
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                uint32_t sc[32];
+                tmem_ld32(tS + c0, sc);
+                tc_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 32; c++) {
+                    const float v = (masked && c0 + c >= kmax) ? -INFINITY : __uint_as_float(sc[c]);
+                    mt8[c & 7] = fmaxf(mt8[c & 7], v);
+                }
             }
             const float mt = fmaxf(fmaxf(fmaxf(mt8[0], mt8[1]), fmaxf(mt8[2], mt8[3])),
-                                   fmaxf(fmaxf(mt8[4], mt8[5]), fmaxf(mt8[6], mt8[7])));
-            const float mn = fmaxf(m, mt);
-            const float mref = mn == -INFINITY ? 0.f : mn;
-            const float alpha = fast_exp2(m - mref);
+                                   fmaxf(fmaxf(mt8[4], mt8[5]), fmaxf(mt8[6], mt8[7]))) * sl2;
+            // this warpgroup's 64 columns
+            uint32_t sr[64];
+            tmem_ld32(tS + cb, sr);
+            tmem_ld32(tS + cb + 32, sr + 32);
+            tc_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_SFREE));
+            if (masked) {
+#pragma unroll
+                for (int c = 0; c < 64; c++)
+                    if (cb + c >= kmax) sr[c] = __float_as_uint(-INFINITY);
+            }
+            // lazy rescaling: keep the stale max unless the new one exceeds it by more than 2^RESCALE_LOG2
+            float alpha = 1.f;
+            if (mt > m + RESCALE_LOG2) {
+                alpha = fast_exp2(m - mt);  // 0 on the first tile (m = -inf)
+                m = mt;
+            }
+            const float mref = m == -INFINITY ? 0.f : m;
             float rs8[8];
 #pragma unroll
             for (int k = 0; k < 8; k++) rs8[k] = 0.f;
 #pragma unroll
-            for (int c = 0; c < BN; c++) {  // eight independent sum chains
-                const float p = fast_exp2(__uint_as_float(sr[c]) - mref);
+            for (int c = 0; c < 64; c++) {  // eight independent sum chains
+                const float p = fast_exp2(fmaf(__uint_as_float(sr[c]), sl2, -mref));
                 rs8[c & 7] += p;
                 sr[c] = __float_as_uint(p);
             }
@@ -212,32 +236,32 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE), (j - 1) & 1));
                 if (!ok) break;
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha < 1.f)) {
+                if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-                    for (int c = 0; c < HD; c += 32) {
+                    for (int c = 0; c < OH; c += 32) {
                         uint32_t orow[32];
-                        tmem_ld32(tO + c, orow);
+                        tmem_ld32(tO + wg * OH + c, orow);
                         tc_wait_ld();
 #pragma unroll
                         for (int k = 0; k < 32; k++) orow[k] = __float_as_uint(__uint_as_float(orow[k]) * alpha);
-                        tmem_st32(tO + c, orow);
+                        tmem_st32(tO + wg * OH + c, orow);
                     }
                     tc_wait_st();
                 }
             }
-            m = mn;
-            // P row r -> shared memory, K-major 128-byte swizzle: 16 chunks of 8 keys, hi and lo parts
+            // this half of P row r -> shared memory (box wg), K-major 128-byte swizzle: 8 chunks of 8 keys
 #pragma unroll
-            for (int cc = 0; cc < BN / 8; cc++) {
+            for (int cc = 0; cc < 8; cc++) {
                 uint32_t hi[4], lo[4];
 #pragma unroll
                 for (int k = 0; k < 4; k++) {
-                    const float p0 = __uint_as_float(sr[cc * 8 + 2 * k]), p1 = __uint_as_float(sr[cc * 8 + 2 * k + 1]);
+                    const float p0 = __uint_as_float(sr[cc * 8 + 2 * k]);
+                    const float p1 = __uint_as_float(sr[cc * 8 + 2 * k + 1]);
                     hi[k] = pack_bf16x2(p0, p1);
-                    const float2 h = unpack_bf16x2(hi[k]);
-                    lo[k] = pack_bf16x2(p0 - h.x, p1 - h.y);
+                    const float2 hv = unpack_bf16x2(hi[k]);
+                    lo[k] = pack_bf16x2(p0 - hv.x, p1 - hv.y);
                 }
-                const uint32_t off = (cc >> 3) * BOX + sw128(r, cc & 7);
+                const uint32_t off = wg * BOX + sw128(r, cc);
                 *reinterpret_cast<uint4 *>(sm + C::P_OFF + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
                 *reinterpret_cast<uint4 *>(sm + C::PLO_OFF + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
             }
@@ -248,14 +272,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE), (ntiles - 1) & 1));
         if (!ok) *abort_flag = 1;
+        // the two halves of each row sum meet in the (now idle) P buffer
+        float *lx = reinterpret_cast<float *>(sm + C::P_OFF);
+        lx[wg * BM + r] = l;
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        const float ltot = l + lx[(1 - wg) * BM + r];
         if (ok && ntiles > 0) {
             tc_fence_after();
-            const float inv = 1.f / l;
-            bf16 *dst = out + static_cast<long>(row0 + qrow) * nq * HD + h * HD;
+            const float inv = 1.f / ltot;
+            bf16 *dst = out + static_cast<long>(row0 + qrow) * nq * HD + h * HD + wg * OH;
 #pragma unroll
-            for (int c = 0; c < HD; c += 32) {
+            for (int c = 0; c < OH; c += 32) {
                 uint32_t orow[32];
-                tmem_ld32(tO + c, orow);
+                tmem_ld32(tO + wg * OH + c, orow);
                 tc_wait_ld();
                 if (qrow < seq) {
 #pragma unroll
