@@ -212,6 +212,75 @@ def reference_arm(args, rank, world):
 # GPU arm
 # ------------------------------------------------------------------------------------------------------------
 
+STEP_TAKES = 32
+STEP_WORKLOAD = ("config 5: random-init VoxCPM2-shaped decoding step per GPU, one CUDA graph: 9 DiT passes "
+                 "(10 timesteps, CFG 2.0, 4 layers) -> local encoder (4 layers) -> base LM (28 layers, hidden 2048, "
+                 "SwiGLU 6144) -> FSQ -> residual LM (8 layers); KV slots of 4096, lengths U[330, 4096)")
+
+
+def patches_leg(args, dev, rank, max_over_ranks, sum_over_ranks, barrier):
+    """Config 5: the whole decoding step (oumu_b200.engine) for --step-takes takes per GPU, as one CUDA graph;
+    patches/s over all ranks, device-resident and end to end (the step's noise uploaded from pinned host memory,
+    the new patch and the stop flags read back and waited for every step, as Engine::decode reads `stop`,
+    src/model.rs:785-794)."""
+    import torch
+    from oumu_b200 import engine, synth
+    B, K, W = args.step_takes, args.step_steps, max(3, min(args.warmup, 5))
+    margin = 2 * (K + W) + 4  # every replay advances every take by one position; lengths reset between legs
+    lens = synth.uniform_int(synth.config_seed(5) + 1000 * rank, B, LEN_LO, MAXLEN - margin)
+    e = engine.Engine(B, maxlen=MAXLEN, max_steps=4 * (K + W) + 8, device=dev)
+    e.prime(lens, seed=5 + rank)
+    from oumu_b200 import _lib
+    c0 = _lib.CALLS[0]
+    graph = e.capture()  # one eager step + the capture: each of this library's launches is called twice
+    launches = (_lib.CALLS[0] - c0) // 2
+
+    def timed(fn):
+        e.set_lens(lens)
+        for _ in range(W):
+            fn()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(K):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(a.elapsed_time(b))
+
+    ms = timed(graph.replay)
+    noise_host = torch.empty((B, engine.PATCH), dtype=torch.bfloat16).pin_memory()
+    noise_host.normal_()
+    patch_host = torch.empty((B, engine.PATCH), dtype=torch.bfloat16).pin_memory()
+    stop_host = torch.empty((B,), dtype=torch.int32).pin_memory()
+    stream = torch.cuda.current_stream()
+
+    def e2e_step():
+        e.noise.copy_(noise_host, non_blocking=True)
+        graph.replay()
+        patch_host.copy_(e.cond, non_blocking=True)  # cond holds this step's patch after the step
+        stop_host.copy_(e.stop, non_blocking=True)
+        stream.synchronize()
+
+    e2e_ms = timed(e2e_step)
+    patches = sum_over_ranks(B * K)
+    kv = 2 * 2 * 128 * 2 * (len(e.base.layers) + len(e.res.layers)) * int(sum(int(v) + W + K // 2 for v in lens))
+    wbytes = e.step_weight_bytes()
+    flops = e.step_flops()
+    del graph
+    return {
+        "value": round(patches / (ms / 1e3), 1), "unit": "patches/s", "takes_per_gpu": B, "steps": K, "warmup": W,
+        "ms_per_step": round(ms / K, 4), "workload": STEP_WORKLOAD, "scaling": "weak",
+        "layers": {"base": len(e.base.layers), "residual": len(e.res.layers), "encoder": len(e.enc.layers),
+                   "dit": len(e.dit.layers), "dit_passes": len(e.sched)},
+        "per_step_per_gpu": {"weight_bytes": wbytes, "kv_bytes_mean": kv, "gemm_flops": flops},
+        "e2e": {"value": round(patches / (e2e_ms / 1e3), 1), "unit": "patches/s",
+                "h2d_bytes_per_step": noise_host.numel() * 2, "d2h_bytes_per_step": B * (engine.PATCH * 2 + 4),
+                "ms_per_step": round(e2e_ms / K, 4),
+                "path": "pinned host noise -> device, graph replay, patch + stop flags -> pinned host, host sync"},
+        "gpu_launches_per_step": launches,
+    }
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -219,6 +288,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-step", action="store_true", help="skip the end-to-end decoding-step leg (patches/s)")
+    ap.add_argument("--step-takes", type=int, default=STEP_TAKES, help="takes per GPU of the decoding-step leg")
+    ap.add_argument("--step-steps", type=int, default=30, help="timed decoding steps of the decoding-step leg")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))
@@ -350,6 +422,8 @@ def main():
     errword = ops.device_error()
     barrier()
 
+    step = None if args.no_step else patches_leg(args, dev, rank, max_over_ranks, sum_over_ranks, barrier)
+
     cpu_base = None
     if world == 1 and not args.no_cpu:
         gbs, thr, secs, sample = cpu_time(lens, 2, 10.0)
@@ -378,6 +452,7 @@ def main():
             "clocks": clocks.summary(),
             "gpu_launches": LAYERS * args.steps,
             "device_error": errword,
+            "patches_per_s": step,
         }
         print(json.dumps(line), flush=True)
     del graph

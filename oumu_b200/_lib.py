@@ -1,4 +1,4 @@
-"""ctypes binding of the C ABI in include/oumu_attn.h (liboumu_attn.so, built in-tree by oumu_b200/build.py).
+"""ctypes binding of the C ABI in include/oumu_attn.h and include/oumu_step.h (liboumu_attn.so, built in-tree by oumu_b200/build.py).
 
 Loading fails loudly when the library is missing: there is no CPU or eager fallback anywhere in this package.
 """
@@ -14,8 +14,9 @@ _P = ctypes.c_void_p
 _I = ctypes.c_int
 _F = ctypes.c_float
 _Z = ctypes.c_size_t
+_L = ctypes.c_long
 
-# name -> (restype, argtypes); the exact declarations of include/oumu_attn.h
+# name -> (restype, argtypes); the exact declarations of include/oumu_attn.h and include/oumu_step.h
 SIGNATURES = {
     "oumu_status_string": (ctypes.c_char_p, [_I]),
     "oumu_last_cuda_error": (ctypes.c_char_p, []),
@@ -32,6 +33,12 @@ SIGNATURES = {
     "oumu_kv_replicate": (_I, [_P, _I, _I, _I, _I, _I, _P]),
     "oumu_device_error": (_I, [_I]),
     "oumu_set_pdl": (_I, [_I]),
+    "oumu_rmsnorm": (_I, [_P, _P, _P, _P, _I, _I, _F, _P]),
+    "oumu_silu_mul": (_I, [_P, _P, _I, _I, _P]),
+    "oumu_pointwise": (_I, [_P, _L, _I, _F, _P]),
+    "oumu_build_seq": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "oumu_cfg_euler": (_I, [_P, _P, _I, _I, _I, _F, _F, _P]),
+    "oumu_step_end": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P]),
 }
 
 _lib = None
@@ -69,8 +76,13 @@ def check(fn, status):
         raise OumuError(fn, status)
 
 
+# entry-point calls made through call() (each launches at most one kernel); read by the benchmark to count launches
+CALLS = [0]
+
+
 def call(name, *args):
     """Call entry point `name` and raise OumuError on a non-zero status."""
+    CALLS[0] += 1
     st = getattr(load(), name)(*args)
     check(name, st)
     return st

@@ -1,7 +1,7 @@
 """Build the sm_100a attention library in-tree: oumu_b200/liboumu_attn.so.
 
 Usage: python -m oumu_b200.build [--force] [--verbose]
-Plain nvcc, no torch extension machinery: the library exposes only the C ABI of include/oumu_attn.h.
+Plain nvcc, no torch extension machinery: the library exposes only the C ABI of include/oumu_attn.h and include/oumu_step.h.
 """
 import os
 import subprocess
@@ -18,7 +18,8 @@ ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 def _sources():
     srcs = [os.path.join(CSRC, f) for f in sorted(os.listdir(CSRC)) if f.endswith((".cu", ".cuh", ".h", ".cpp"))]
-    return srcs + [os.path.join(ROOT, "include", "oumu_attn.h")]
+    inc = os.path.join(ROOT, "include")
+    return srcs + [os.path.join(inc, f) for f in sorted(os.listdir(inc)) if f.endswith(".h")]
 
 
 def stale():

@@ -2,6 +2,7 @@
 // Host side: argument validation, TMA tensor-map encoding, launch shapes. Nothing here allocates, synchronises
 // or reads device memory (except oumu_device_error), so every entry point can be captured in a CUDA graph.
 #include "../../include/oumu_attn.h"
+#include "../../include/oumu_step.h"
 
 #include <atomic>
 #include <cmath>
@@ -15,6 +16,7 @@
 #include "feeders.cuh"
 #include "full_small.cuh"
 #include "prefill_tc.cuh"
+#include "step_glue.cuh"
 
 namespace {
 
@@ -459,6 +461,89 @@ int oumu_device_error(int reset) {
         OUMU_CK(cudaMemcpyToSymbol(oumu_dev_error, &z, sizeof(z)));
     }
     return static_cast<int>(v);
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// Step glue (include/oumu_step.h)
+// ------------------------------------------------------------------------------------------------------------
+
+int oumu_rmsnorm(void *res, const void *d, const void *w, void *out, int rows, int dim, float eps,
+                 oumu_stream_t stream) {
+    if (!res || !w || !out || rows < 0) return OUMU_ERR_INVALID;
+    if (dim != 1024 && dim != 2048) return OUMU_ERR_UNSUPPORTED;
+    if (!aligned16(res) || !aligned16(w) || !aligned16(out) || (d && !aligned16(d))) return OUMU_ERR_INVALID;
+    if (rows == 0) return OUMU_OK;
+    const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+    if (dim == 1024)
+        glue::k_rmsnorm<1024><<<grid, 256, 0, stream>>>(static_cast<bf16 *>(res), static_cast<const bf16 *>(d),
+                                                        static_cast<const bf16 *>(w), static_cast<bf16 *>(out), rows,
+                                                        eps);
+    else
+        glue::k_rmsnorm<2048><<<grid, 256, 0, stream>>>(static_cast<bf16 *>(res), static_cast<const bf16 *>(d),
+                                                        static_cast<const bf16 *>(w), static_cast<bf16 *>(out), rows,
+                                                        eps);
+    OUMU_CK(cudaGetLastError());
+    return OUMU_OK;
+}
+
+int oumu_silu_mul(const void *gu, void *out, int rows, int F, oumu_stream_t stream) {
+    if (!gu || !out || rows < 0 || F < 8 || F % 8) return OUMU_ERR_INVALID;
+    if (!aligned16(gu) || !aligned16(out)) return OUMU_ERR_INVALID;
+    const long vecs = static_cast<long>(rows) * (F / 8);
+    if (vecs == 0) return OUMU_OK;
+    glue::k_silu_mul<<<static_cast<unsigned>((vecs + 255) / 256), 256, 0, stream>>>(
+        static_cast<const bf16 *>(gu), static_cast<bf16 *>(out), rows, F);
+    OUMU_CK(cudaGetLastError());
+    return OUMU_OK;
+}
+
+int oumu_pointwise(void *x, long n, int op, float scale, oumu_stream_t stream) {
+    if (!x || n < 0 || n % 8 || (op != 0 && op != 1) || !aligned16(x)) return OUMU_ERR_INVALID;
+    if (op == 1 && !(scale != 0.f)) return OUMU_ERR_INVALID;
+    if (n == 0) return OUMU_OK;
+    const long vecs = n / 8;
+    glue::k_pointwise<<<static_cast<unsigned>((vecs + 255) / 256), 256, 0, stream>>>(static_cast<bf16 *>(x), n, op,
+                                                                                     scale);
+    OUMU_CK(cudaGetLastError());
+    return OUMU_OK;
+}
+
+int oumu_build_seq(void *seq_out, const void *mu, const void *temb, const void *condp, const void *xp, int rows,
+                   int B, int seq, int H, oumu_stream_t stream) {
+    if (!seq_out || !temb || !xp || rows < 0 || H < 8 || H % 8) return OUMU_ERR_INVALID;
+    if (seq == 11) {
+        if (!mu || !condp || B < 0 || rows != 2 * B || !aligned16(mu) || !aligned16(condp)) return OUMU_ERR_INVALID;
+    } else if (seq != 5) {
+        return OUMU_ERR_UNSUPPORTED;
+    }
+    if (!aligned16(seq_out) || !aligned16(temb) || !aligned16(xp)) return OUMU_ERR_INVALID;
+    const long vecs = static_cast<long>(rows) * seq * (H / 8);
+    if (vecs == 0) return OUMU_OK;
+    glue::k_build_seq<<<static_cast<unsigned>((vecs + 255) / 256), 256, 0, stream>>>(
+        static_cast<bf16 *>(seq_out), static_cast<const bf16 *>(mu), static_cast<const bf16 *>(temb),
+        static_cast<const bf16 *>(condp), static_cast<const bf16 *>(xp), rows, B, seq, H);
+    OUMU_CK(cudaGetLastError());
+    return OUMU_OK;
+}
+
+int oumu_cfg_euler(void *x, const void *out, int B, int seq, int first, float dt, float cfg, oumu_stream_t stream) {
+    if (!x || !out || B < 0 || seq < 4 || first < 0 || first + 4 > seq) return OUMU_ERR_INVALID;
+    if (B == 0) return OUMU_OK;
+    glue::k_cfg_euler<<<static_cast<unsigned>(B), 256, 0, stream>>>(static_cast<bf16 *>(x),
+                                                                    static_cast<const bf16 *>(out), B, seq, first,
+                                                                    dt, cfg);
+    OUMU_CK(cudaGetLastError());
+    return OUMU_OK;
+}
+
+int oumu_step_end(const void *stop_logits, const void *patch, void *patches, int *stop, int *ctr, int *lens, int B,
+                  int min_len, int max_steps, oumu_stream_t stream) {
+    if (!stop_logits || !patch || !patches || !stop || !ctr || B < 0 || max_steps < 1) return OUMU_ERR_INVALID;
+    if (!aligned16(patch) || !aligned16(patches)) return OUMU_ERR_INVALID;
+    glue::k_step_end<<<1, 256, 0, stream>>>(static_cast<const bf16 *>(stop_logits), static_cast<const bf16 *>(patch),
+                                            static_cast<bf16 *>(patches), stop, ctr, lens, B, min_len, max_steps);
+    OUMU_CK(cudaGetLastError());
+    return OUMU_OK;
 }
 
 }  // extern "C"

@@ -1,0 +1,201 @@
+// Element-wise and per-row kernels of the decoding step around the attention (the step's glue): RMS norms, the
+// SwiGLU product, the DiT and local-encoder input sequences, classifier-free guidance with the Euler update, the
+// FSQ activation and the step end. Each has the rounding points of the reference kernel it stands in for
+// (kernels/voxcpm.cu), so a step built from them tracks the reference step; the layouts are this library's own:
+// every kernel moves 16-byte vectors, and row norms run one warp per row with the row held in registers.
+#pragma once
+#include "common.cuh"
+
+namespace glue {
+
+__device__ __forceinline__ float rbf(float x) { return bf2f(f2bf(x)); }
+
+__device__ __forceinline__ void load8(const bf16 *p, float *v) {
+    uint4 u = *reinterpret_cast<const uint4 *>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        float2 f = unpack_bf16x2(w[j]);
+        v[2 * j] = f.x;
+        v[2 * j + 1] = f.y;
+    }
+}
+__device__ __forceinline__ void store8(bf16 *p, const float *v) {
+    uint4 u;
+    u.x = pack_bf16x2(v[0], v[1]);
+    u.y = pack_bf16x2(v[2], v[3]);
+    u.z = pack_bf16x2(v[4], v[5]);
+    u.w = pack_bf16x2(v[6], v[7]);
+    *reinterpret_cast<uint4 *>(p) = u;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// One warp per row of DIM elements, DIM/256 vectors of 8 per lane, kept in registers between the sum of squares
+// and the scaling. With `d`: res = bf16(res + d) first (add_rmsnorm, kernels/voxcpm.cu:55-67), else rmsnorm
+// (kernels/voxcpm.cu:43-52). out = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w).
+template <int DIM>
+__global__ void __launch_bounds__(256) k_rmsnorm(bf16 *res, const bf16 *d, const bf16 *w, bf16 *out, int rows,
+                                                 float eps) {
+    constexpr int VPL = DIM / 256;
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    bf16 *xr = res + static_cast<long>(row) * DIM;
+    float v[VPL][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; i++) {
+        const int c = (i * 32 + lane) * 8;
+        load8(xr + c, v[i]);
+        if (d) {
+            float dv[8];
+            load8(d + static_cast<long>(row) * DIM + c, dv);
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[i][j] = rbf(v[i][j] + dv[j]);
+            store8(xr + c, v[i]);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) ss += v[i][j] * v[i][j];
+    }
+    const float r = rsqrtf(warp_sum(ss) / DIM + eps);
+    bf16 *yr = out + static_cast<long>(row) * DIM;
+#pragma unroll
+    for (int i = 0; i < VPL; i++) {
+        const int c = (i * 32 + lane) * 8;
+        float wv[8], o[8];
+        load8(w + c, wv);
+#pragma unroll
+        for (int j = 0; j < 8; j++) o[j] = rbf(v[i][j] * r) * wv[j];
+        store8(yr + c, o);
+    }
+}
+
+// out[r, c] = bf16(bf16(silu(gate)) * up) with gu = [gate | up] per row, F columns each (kernels/voxcpm.cu:92-99).
+__global__ void __launch_bounds__(256) k_silu_mul(const bf16 *gu, bf16 *out, int rows, int F) {
+    const long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;  // vector index
+    const int fv = F / 8;
+    if (i >= static_cast<long>(rows) * fv) return;
+    const long r = i / fv;
+    const int c = static_cast<int>(i - r * fv) * 8;
+    float g[8], u[8], o[8];
+    load8(gu + r * 2 * F + c, g);
+    load8(gu + r * 2 * F + F + c, u);
+#pragma unroll
+    for (int j = 0; j < 8; j++) o[j] = rbf(g[j] / (1.f + __expf(-g[j]))) * u[j];
+    store8(out + r * F + c, o);
+}
+
+// In place over n elements (n % 8 == 0): op 0 = silu (kernels/voxcpm.cu:80-83); op 1 = FSQ,
+// h = bf16(rint(bf16(bf16(tanh(h)) * scale)) / scale) (kernels/voxcpm.cu:370-375).
+__global__ void __launch_bounds__(256) k_pointwise(bf16 *x, long n, int op, float scale) {
+    const long i = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+    if (i >= n) return;
+    float v[8];
+    load8(x + i, v);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        if (op == 0) {
+            v[j] = v[j] / (1.f + __expf(-v[j]));
+        } else {
+            const float t = rbf(tanhf(v[j]));
+            v[j] = rintf(rbf(t * scale)) / scale;
+        }
+    }
+    store8(x + i, v);
+}
+
+// DiT input sequences [mu0, mu1, t, cond x4, x x4] for 2B rows (kernels/voxcpm.cu:299-315): rows < B carry
+// mu = [B][2][H], rows >= B zeros (the unconditional branch); condp and xp are [B][4][H], shared by both halves.
+// With seq == 5 and mu == null: the local encoder's [special, x0..x3] per patch (kernels/voxcpm.cu:325-331),
+// `temb` then being the special token and rows = n patches.
+__global__ void __launch_bounds__(256) k_build_seq(bf16 *seq_out, const bf16 *mu, const bf16 *temb,
+                                                   const bf16 *condp, const bf16 *xp, int rows, int B, int seq,
+                                                   int H) {
+    const long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int hv = H / 8;
+    if (i >= static_cast<long>(rows) * seq * hv) return;
+    const int c = static_cast<int>(i % hv) * 8;
+    const long rt = i / hv;
+    const int tok = static_cast<int>(rt % seq);
+    const int r = static_cast<int>(rt / seq);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (seq == 5) {
+        v = tok == 0 ? *reinterpret_cast<const uint4 *>(temb + c)
+                     : *reinterpret_cast<const uint4 *>(xp + (static_cast<long>(r) * 4 + tok - 1) * H + c);
+    } else {
+        const int s = r % B;
+        if (tok < 2) {
+            if (r < B) v = *reinterpret_cast<const uint4 *>(mu + (static_cast<long>(s) * 2 + tok) * H + c);
+        } else if (tok == 2) {
+            v = *reinterpret_cast<const uint4 *>(temb + c);
+        } else if (tok < 7) {
+            v = *reinterpret_cast<const uint4 *>(condp + (static_cast<long>(s) * 4 + tok - 3) * H + c);
+        } else {
+            v = *reinterpret_cast<const uint4 *>(xp + (static_cast<long>(s) * 4 + tok - 7) * H + c);
+        }
+    }
+    *reinterpret_cast<uint4 *>(seq_out + rt * H + c) = v;
+}
+
+// Block-wide sum over 256 threads.
+__device__ __forceinline__ float block_sum256(float v, float *red) {
+    v = warp_sum(v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; k++) t += red[k];
+    return t;
+}
+
+// Classifier-free guidance (CFG-Zero*) and one Euler step for take s (block s, 256 threads = 4 frames x 64
+// channels), the roundings of kernels/voxcpm.cu:334-345. The DiT output rows are read where they lie: frame t of
+// row r at out[((r * seq + first + t) * 64 + c)], so the noisy-frame tokens need not be gathered first.
+__global__ void __launch_bounds__(256) k_cfg_euler(bf16 *x, const bf16 *out, int B, int seq, int first, float dt,
+                                                   float cfg) {
+    __shared__ float red[8];
+    const int s = blockIdx.x, i = threadIdx.x, t = i >> 6, c = i & 63;
+    const float pos = bf2f(out[((static_cast<long>(s) * seq + first + t) << 6) + c]);
+    const float neg = bf2f(out[((static_cast<long>(B + s) * seq + first + t) << 6) + c]);
+    const float dot = rbf(block_sum256(rbf(pos * neg), red));
+    const float nn = rbf(rbf(block_sum256(rbf(neg * neg), red)) + 1e-8f);
+    const float st = rbf(dot / nn);
+    const float a = rbf(neg * st);
+    const float dv = rbf(a + rbf(cfg * rbf(pos - a)));
+    const long xi = static_cast<long>(s) * 256 + i;
+    x[xi] = f2bf(bf2f(x[xi]) - rbf(dt * dv));
+}
+
+// End of a decoding step (kernels/voxcpm.cu:415-433), one block: the new patch of every take goes to
+// patches[s][n] (n = ctr[1] < max_steps), a take whose stop logits ask to stop after more than min_len patches
+// records n, then ctr = [position + 1, n + 1] and, with per-take lengths, every lens[s] + 1.
+__global__ void __launch_bounds__(256) k_step_end(const bf16 *stop_logits, const bf16 *patch, bf16 *patches,
+                                                  int *stop, int *ctr, int *lens, int B, int min_len,
+                                                  int max_steps) {
+    const int n = ctr[1];
+    if (n < max_steps) {
+        for (int v = threadIdx.x; v < B * 32; v += blockDim.x) {
+            const int s = v >> 5, e = (v & 31) * 8;
+            *reinterpret_cast<uint4 *>(patches + (static_cast<long>(s) * max_steps + n) * 256 + e) =
+                *reinterpret_cast<const uint4 *>(patch + static_cast<long>(s) * 256 + e);
+        }
+    }
+    for (int s = threadIdx.x; s < B; s += blockDim.x) {
+        const bool want = bf2f(stop_logits[2 * s + 1]) > bf2f(stop_logits[2 * s]);
+        if (want && n > min_len && stop[s] < 0) stop[s] = n;
+        if (lens) lens[s] += 1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        ctr[0] += 1;
+        ctr[1] = n + 1;
+    }
+}
+
+}  // namespace glue

@@ -130,3 +130,45 @@ def full_attention(qkv, att, rows, seq, causal, nq, nk, hd, maxlen=0, cos_t=None
     if kc is not None:
         kv_write(qkv, kc, vc, None, 1, rows, nq, nk, hd, maxlen)
     attn_full(qkv, att, rows, seq, causal, nq, nk, hd, 1.0 / hd ** 0.5)
+
+
+# ------------------------------------------------------------------------------------------------------------
+# Step glue (include/oumu_step.h): the per-row and element-wise kernels between the GEMMs of a step
+# ------------------------------------------------------------------------------------------------------------
+
+def rmsnorm(res, w, out, eps, d=None):
+    """out = rmsnorm(res) * w; with d, res += d first (add_rmsnorm). res/out [rows][dim], dim 1024 or 2048."""
+    _lib.call("oumu_rmsnorm", _p(res), _p(d), _p(w), _p(out), res.shape[0], res.shape[-1], eps, _stream())
+    return out
+
+
+def silu_mul(gu, out):
+    """out [rows][F] = bf16(bf16(silu(gate)) * up) of gu = [gate | up] [rows][2F]."""
+    _lib.call("oumu_silu_mul", _p(gu), _p(out), gu.shape[0], gu.shape[-1] // 2, _stream())
+    return out
+
+
+def silu_(x):
+    _lib.call("oumu_pointwise", _p(x), x.numel(), 0, 1.0, _stream())
+    return x
+
+
+def fsq_(x, scale=9.0):
+    _lib.call("oumu_pointwise", _p(x), x.numel(), 1, scale, _stream())
+    return x
+
+
+def build_seq(seq_out, temb, xp, rows, seq, H, mu=None, condp=None, B=0):
+    """DiT (seq 11, rows = 2B) or local-encoder (seq 5, temb = the special token) input sequences."""
+    _lib.call("oumu_build_seq", _p(seq_out), _p(mu), _p(temb), _p(condp), _p(xp), rows, B, seq, H, _stream())
+    return seq_out
+
+
+def cfg_euler(x, out, B, seq, first, dt, cfg):
+    _lib.call("oumu_cfg_euler", _p(x), _p(out), B, seq, first, dt, cfg, _stream())
+    return x
+
+
+def step_end(stop_logits, patch, patches, stop, ctr, lens, B, min_len, max_steps):
+    _lib.call("oumu_step_end", _p(stop_logits), _p(patch), _p(patches), _p(stop), _p(ctr), _p(lens), B, min_len,
+              max_steps, _stream())

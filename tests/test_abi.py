@@ -1,4 +1,4 @@
-"""The C-ABI library: it loads, exports every entry point include/oumu_attn.h declares, rejects invalid arguments
+"""The C-ABI library: it loads, exports every entry point include/*.h declares, rejects invalid arguments
 on the host before touching the GPU, and builds the rotary tables bit-exactly like the reference (no GPU needed)."""
 import ctypes
 import os
@@ -11,11 +11,11 @@ from oumu_b200 import _lib, build
 from oracle import cpu
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADER = os.path.join(ROOT, "include", "oumu_attn.h")
+HEADERS = [os.path.join(ROOT, "include", f) for f in ("oumu_attn.h", "oumu_step.h")]
 
 
 def declarations():
-    text = open(HEADER).read()
+    text = "\n".join(open(h).read() for h in HEADERS)
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     out = {}
     for m in re.finditer(r"(?:^|\n)\s*(?:const\s+)?[a-z_]+\s*\*?\s*(oumu_[a-z0-9_]+)\s*\(([^;]*?)\)\s*;", text):
@@ -34,7 +34,7 @@ def test_every_declared_symbol_is_exported(lib):
     decl = declarations()
     assert len(decl) >= 12, decl
     for name, nargs in decl.items():
-        assert hasattr(lib, name), f"{name} declared in oumu_attn.h but not exported"
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
         assert name in _lib.SIGNATURES, f"{name} missing from the ctypes table"
         assert len(_lib.SIGNATURES[name][1]) == nargs, f"{name}: {nargs} C parameters"
     assert set(_lib.SIGNATURES) <= set(decl)
