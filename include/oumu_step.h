@@ -66,6 +66,17 @@ int oumu_cfg_euler(void *x, const void *out, int B, int seq, int first, float dt
 int oumu_step_end(const void *stop_logits, const void *patch, void *patches, int *stop, int *ctr, int *lens, int B,
                   int min_len, int max_steps, oumu_stream_t stream);
 
+/*
+ * y[m][n] (row pitch ldy) = bf16(sum_k x[m][k] * W[n][k] (+ bias[n])) for m < M, n < N: x bf16 [M][K] with row
+ * pitch ldx (>= K, a multiple of 8), W bf16 [N][K] contiguous, bias bf16 [N] or NULL, fp32 accumulation, one
+ * rounding after the bias. K must be a multiple of 64; x and W 16-byte aligned. Replaces Lin::fwd -> Gpu::gemm
+ * (src/model.rs:27-45, src/gpu.rs:186-229: gemv_* for M <= 8, cuBLAS gemm_ex above; fill_bias + beta = 1,
+ * kernels/voxcpm.cu:70-76). One launch of thread-block clusters, no workspace, deterministic; with oumu_set_pdl(1)
+ * it may start during the preceding kernel and stream its first weights before waiting for it.
+ */
+int oumu_gemm(const void *x, int ldx, const void *w, void *y, int ldy, const void *bias, int M, int N, int K,
+              oumu_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

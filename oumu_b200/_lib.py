@@ -39,6 +39,7 @@ SIGNATURES = {
     "oumu_build_seq": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "oumu_cfg_euler": (_I, [_P, _P, _I, _I, _I, _F, _F, _P]),
     "oumu_step_end": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P]),
+    "oumu_gemm": (_I, [_P, _I, _P, _P, _I, _P, _I, _I, _I, _P]),
 }
 
 _lib = None

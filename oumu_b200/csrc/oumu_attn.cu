@@ -15,6 +15,7 @@
 #include "decode.cuh"
 #include "feeders.cuh"
 #include "full_small.cuh"
+#include "gemm_tc.cuh"
 #include "prefill_tc.cuh"
 #include "step_glue.cuh"
 
@@ -53,6 +54,10 @@ cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
 }
 
 constexpr int kMaxDevices = 64;
+// Weight-streaming GEMM: pipeline depth per token tile (shared memory: stages x (16 KB + tile x 128 B) + the
+// inbox).
+constexpr int kGemmStages32 = 4, kGemmStages64 = 4, kGemmStages128 = 3;
+
 constexpr int kSmemMax = 227 * 1024;
 
 struct DevInfo {
@@ -84,6 +89,12 @@ int current_device(int *sms) {
                                      pf::Cfg<128>::SMEM));
         OUMU_CK(cudaFuncSetAttribute(pf::k_attn_prefill<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      pf::Cfg<64>::SMEM));
+        OUMU_CK(cudaFuncSetAttribute(gm::k_gemm<32, kGemmStages32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(gm::k_gemm<64, kGemmStages64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(gm::k_gemm<128, kGemmStages128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
         di.ready = true;
     }
     *sms = di.sms;
@@ -221,6 +232,110 @@ int launch_prefill(const void *qkv, void *out, int rows, int seq, int causal, in
     pf::k_attn_prefill<HD><<<grid, pf::NTHREADS, pf::Cfg<HD>::SMEM, st>>>(
         tm, static_cast<bf16 *>(out), seq, causal, nq, nk, scale * 1.4426950408889634f);
     OUMU_CK(cudaGetLastError());
+    return OUMU_OK;
+}
+
+// Token tile of the GEMM for M tokens, the tile counts and the K split (CTAs per output tile = the cluster size).
+struct GemmShape {
+    int tn, tt, nt, kb, split;
+    long tiles;
+};
+
+GemmShape gemm_shape(int M, int N, int K) {
+    GemmShape g;
+    g.tn = M <= 32 ? 32 : (M <= 64 ? 64 : 128);
+    g.tt = (M + g.tn - 1) / g.tn;
+    g.nt = (N + gm::BW - 1) / gm::BW;
+    g.kb = K / gm::BK;
+    g.tiles = static_cast<long>(g.tt) * g.nt;
+    g.split = 1;
+    return g;
+}
+
+// Clusters of `split` CTAs of k_gemm<TN, STAGES> resident at once on the current device (occupancy query, cached
+// per device and split; 0 if the query fails). A kernel that allocates TMEM runs one CTA per SM.
+template <int TN, int STAGES>
+int gemm_capacity(int dev, int split) {
+    static int cache[kMaxDevices][gm::MAX_SPLIT + 1];
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    int &c = cache[dev][split];
+    if (c == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(split * 1024));
+        cfg.blockDim = dim3(gm::NTHREADS);
+        cfg.dynamicSmemBytes = gm::Cfg<TN, STAGES>::smem_bytes(split);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = static_cast<unsigned>(split);
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void *>(gm::k_gemm<TN, STAGES>), &cfg) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            n = -1;
+        }
+        c = n;
+    }
+    return c > 0 ? c : 0;
+}
+
+// The largest split (at most 8, at most one per K block) whose grid is resident in one wave; 1 when even that
+// does not fit (many tiles: the DiT's token counts).
+template <int TN, int STAGES>
+void gemm_pick_split(GemmShape &g, int dev) {
+    g.split = 1;
+    const int hi = g.kb < gm::MAX_SPLIT ? g.kb : gm::MAX_SPLIT;
+    for (int sp = hi; sp >= 2; sp--) {
+        if (g.tiles <= gemm_capacity<TN, STAGES>(dev, sp)) {
+            g.split = sp;
+            return;
+        }
+    }
+}
+
+bool gemm_args_ok(const void *x, int ldx, const void *w, const void *y, int ldy, int M, int N, int K) {
+    return x && w && y && M >= 1 && N >= 1 && K >= gm::BK && K % gm::BK == 0 && ldx >= K && ldx % 8 == 0 &&
+           ldy >= N && aligned16(x) && aligned16(w);
+}
+
+template <int TN, int STAGES>
+int launch_gemm(const void *x, int ldx, const void *w, void *y, int ldy, const void *bias, int M, int N, int K,
+                GemmShape gs, int dev, cudaStream_t st) {
+    gemm_pick_split<TN, STAGES>(gs, dev);
+    if (gs.tiles * gs.split > 0x7fffffffL) return OUMU_ERR_UNSUPPORTED;
+    CUtensorMap tw, tx;
+    int rc = make_map(&tw, w, K, N, static_cast<uint64_t>(K) * 2, gm::BK, gm::BW);
+    if (rc) return rc;
+    rc = make_map(&tx, x, K, M, static_cast<uint64_t>(ldx) * 2, gm::BK, TN);
+    if (rc) return rc;
+    gm::Params P;
+    P.y = static_cast<bf16 *>(y);
+    P.bias = static_cast<const bf16 *>(bias);
+    P.ldy = ldy;
+    P.M = M;
+    P.N = N;
+    P.NT = gs.nt;
+    P.KB = gs.kb;
+    P.split = gs.split;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(gs.tiles * gs.split));
+    cfg.blockDim = dim3(gm::NTHREADS);
+    cfg.dynamicSmemBytes = gm::Cfg<TN, STAGES>::smem_bytes(gs.split);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(gs.split);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = g_pdl.load(std::memory_order_relaxed) ? 2 : 1;
+    OUMU_CK(cudaLaunchKernelEx(&cfg, gm::k_gemm<TN, STAGES>, tw, tx, P));
     return OUMU_OK;
 }
 
@@ -473,9 +588,9 @@ int oumu_rmsnorm(void *res, const void *d, const void *w, void *out, int rows, i
     if (dim != 1024 && dim != 2048) return OUMU_ERR_UNSUPPORTED;
     if (!aligned16(res) || !aligned16(w) || !aligned16(out) || (d && !aligned16(d))) return OUMU_ERR_INVALID;
     if (rows == 0) return OUMU_OK;
-    const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+    const unsigned grid = static_cast<unsigned>(rows);
     if (dim == 1024)
-        glue::k_rmsnorm<1024><<<grid, 256, 0, stream>>>(static_cast<bf16 *>(res), static_cast<const bf16 *>(d),
+        glue::k_rmsnorm<1024><<<grid, 128, 0, stream>>>(static_cast<bf16 *>(res), static_cast<const bf16 *>(d),
                                                         static_cast<const bf16 *>(w), static_cast<bf16 *>(out), rows,
                                                         eps);
     else
@@ -544,6 +659,20 @@ int oumu_step_end(const void *stop_logits, const void *patch, void *patches, int
                                             static_cast<bf16 *>(patches), stop, ctr, lens, B, min_len, max_steps);
     OUMU_CK(cudaGetLastError());
     return OUMU_OK;
+}
+
+int oumu_gemm(const void *x, int ldx, const void *w, void *y, int ldy, const void *bias, int M, int N, int K,
+              oumu_stream_t stream) {
+    if (!gemm_args_ok(x, ldx, w, y, ldy, M, N, K)) return OUMU_ERR_INVALID;
+    int sms = 0, dev = 0;
+    int rc = current_device(&sms);
+    if (rc) return rc;
+    OUMU_CK(cudaGetDevice(&dev));
+    const GemmShape gs = gemm_shape(M, N, K);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (gs.tn == 32) return launch_gemm<32, kGemmStages32>(x, ldx, w, y, ldy, bias, M, N, K, gs, dev, st);
+    if (gs.tn == 64) return launch_gemm<64, kGemmStages64>(x, ldx, w, y, ldy, bias, M, N, K, gs, dev, st);
+    return launch_gemm<128, kGemmStages128>(x, ldx, w, y, ldy, bias, M, N, K, gs, dev, st);
 }
 
 }  // extern "C"

@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
             }
         }
+        __syncwarp();  // the warp reaches the final CTA barrier converged
     } else if (warp == 1) {
         // ------------------------------ MMA issuer ------------------------------
         if (lane == 0) {

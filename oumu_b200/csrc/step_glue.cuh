@@ -2,7 +2,7 @@
 // SwiGLU product, the DiT and local-encoder input sequences, classifier-free guidance with the Euler update, the
 // FSQ activation and the step end. Each has the rounding points of the reference kernel it stands in for
 // (kernels/voxcpm.cu), so a step built from them tracks the reference step; the layouts are this library's own:
-// every kernel moves 16-byte vectors, and row norms run one warp per row with the row held in registers.
+// every kernel moves 16-byte vectors, and row norms run one block per row with the row held in registers.
 #pragma once
 #include "common.cuh"
 
@@ -35,44 +35,42 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-// One warp per row of DIM elements, DIM/256 vectors of 8 per lane, kept in registers between the sum of squares
-// and the scaling. With `d`: res = bf16(res + d) first (add_rmsnorm, kernels/voxcpm.cu:55-67), else rmsnorm
-// (kernels/voxcpm.cu:43-52). out = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w).
+// One block per row of DIM elements, DIM/8 threads, one 16-byte vector each: rows spread over the SMs, and the
+// row, its residual and the norm weights are all in flight at once. With `d`: res = bf16(res + d) first
+// (add_rmsnorm, kernels/voxcpm.cu:55-67), else rmsnorm (kernels/voxcpm.cu:43-52).
+// out = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w).
 template <int DIM>
-__global__ void __launch_bounds__(256) k_rmsnorm(bf16 *res, const bf16 *d, const bf16 *w, bf16 *out, int rows,
-                                                 float eps) {
-    constexpr int VPL = DIM / 256;
-    const int lane = threadIdx.x & 31;
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (row >= rows) return;
-    bf16 *xr = res + static_cast<long>(row) * DIM;
-    float v[VPL][8];
+__global__ void __launch_bounds__(DIM / 8) k_rmsnorm(bf16 *res, const bf16 *d, const bf16 *w, bf16 *out, int rows,
+                                                     float eps) {
+    constexpr int NW = DIM / 256;
+    __shared__ float red[NW];
+    const int c = threadIdx.x * 8;
+    const long row = blockIdx.x;
+    bf16 *xr = res + row * DIM;
+    float v[8], wv[8];
+    load8(xr + c, v);
+    load8(w + c, wv);
+    if (d) {
+        float dv[8];
+        load8(d + row * DIM + c, dv);
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = rbf(v[j] + dv[j]);
+        store8(xr + c, v);
+    }
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < VPL; i++) {
-        const int c = (i * 32 + lane) * 8;
-        load8(xr + c, v[i]);
-        if (d) {
-            float dv[8];
-            load8(d + static_cast<long>(row) * DIM + c, dv);
+    for (int j = 0; j < 8; j++) ss += v[j] * v[j];
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
 #pragma unroll
-            for (int j = 0; j < 8; j++) v[i][j] = rbf(v[i][j] + dv[j]);
-            store8(xr + c, v[i]);
-        }
+    for (int k = 0; k < NW; k++) tot += red[k];
+    const float r = rsqrtf(tot / DIM + eps);
+    float o[8];
 #pragma unroll
-        for (int j = 0; j < 8; j++) ss += v[i][j] * v[i][j];
-    }
-    const float r = rsqrtf(warp_sum(ss) / DIM + eps);
-    bf16 *yr = out + static_cast<long>(row) * DIM;
-#pragma unroll
-    for (int i = 0; i < VPL; i++) {
-        const int c = (i * 32 + lane) * 8;
-        float wv[8], o[8];
-        load8(w + c, wv);
-#pragma unroll
-        for (int j = 0; j < 8; j++) o[j] = rbf(v[i][j] * r) * wv[j];
-        store8(yr + c, o);
-    }
+    for (int j = 0; j < 8; j++) o[j] = rbf(v[j] * r) * wv[j];
+    store8(out + row * DIM + c, o);
 }
 
 // out[r, c] = bf16(bf16(silu(gate)) * up) with gu = [gate | up] per row, F columns each (kernels/voxcpm.cu:92-99).

@@ -70,13 +70,17 @@ class _Init:
 
 
 class Lin:
-    """y = x W^T (+ b), weight [n][k] bf16 (src/model.rs:27-45)."""
+    """y = x W^T (+ b), weight [n][k] bf16 (src/model.rs:27-45). `tc`: through this library's tensor-core GEMM
+    (oumu_gemm) instead of cuBLAS."""
 
-    def __init__(self, ini, n, k, bias):
+    def __init__(self, ini, n, k, bias, tc=False):
         self.w = ini.w(n, k)
         self.b = ini.w(n) if bias else None
+        self.tc = tc
 
     def __call__(self, x, out):
+        if self.tc:
+            return ops.gemm(x, self.w, out, bias=self.b)
         if self.b is None:
             return torch.matmul(x, self.w.t(), out=out)
         return torch.addmm(self.b, x, self.w.t(), out=out)
@@ -89,10 +93,11 @@ class Tf:
     """One transformer stack (src/model.rs:47-63,111-138): per layer ln1, qkv, o, ln2, gate|up, down; final norm;
     with `slots`, one K and one V cache [slots][NK][maxlen][HD] per layer."""
 
-    def __init__(self, ini, n, h, ffn, rope, slots=0, maxlen=0):
+    def __init__(self, ini, n, h, ffn, rope, slots=0, maxlen=0, tc=()):
         self.h, self.ffn, self.rope = h, ffn, rope
-        self.layers = [dict(ln1=ini.norm(h), qkv=Lin(ini, QKV, h, False), o=Lin(ini, h, QW, False), ln2=ini.norm(h),
-                            gu=Lin(ini, 2 * ffn, h, False), down=Lin(ini, h, ffn, False)) for _ in range(n)]
+        self.layers = [dict(ln1=ini.norm(h), qkv=Lin(ini, QKV, h, False, "qkv" in tc), o=Lin(ini, h, QW, False, "o" in tc),
+                            ln2=ini.norm(h), gu=Lin(ini, 2 * ffn, h, False, "gu" in tc),
+                            down=Lin(ini, h, ffn, False, "down" in tc)) for _ in range(n)]
         self.norm = ini.norm(h)
         shape = (slots, NK, maxlen, HD)
         self.kc = [torch.zeros(shape, dtype=torch.bfloat16, device=ini.device) for _ in range(n)] if slots else []
@@ -109,15 +114,19 @@ class Tf:
 class Engine:
     """Weights, KV slots and step buffers for B takes (src/model.rs:184-243, 404-529)."""
 
+    # LM projections that run on this library's GEMM (oumu_gemm) instead of cuBLAS: none by default; inside the
+    # captured step cuBLAS measured 4.75 ms against 4.79 ms with o and down on oumu_gemm (32 takes, B200)
+    LM_TC = ()
+
     def __init__(self, B, maxlen=4096, timesteps=10, base_layers=28, res_layers=8, enc_layers=4, dit_layers=4,
-                 cfg=2.0, max_steps=256, min_len=2, seed=0, device="cuda"):
+                 cfg=2.0, max_steps=256, min_len=2, seed=0, device="cuda", lm_tc=LM_TC):
         if not 1 <= B <= 1024:
             raise ValueError("takes per GPU must be in 1..1024")
         self.B, self.maxlen, self.cfg, self.max_steps, self.min_len = B, maxlen, cfg, max_steps, min_len
         self.device = dev = torch.device(device)
         ini = _Init(seed, dev)
-        self.base = Tf(ini, base_layers, LM, LM_FFN, True, B, maxlen)
-        self.res = Tf(ini, res_layers, LM, LM_FFN, False, B, maxlen)  # residual LM: no rope (src/model.rs:445)
+        self.base = Tf(ini, base_layers, LM, LM_FFN, True, B, maxlen, tc=lm_tc)
+        self.res = Tf(ini, res_layers, LM, LM_FFN, False, B, maxlen, tc=lm_tc)  # no rope (src/model.rs:445)
         self.enc = Tf(ini, enc_layers, LOC, LOC_FFN, True)
         self.dit = Tf(ini, dit_layers, LOC, LOC_FFN, True)
         L = lambda n, k, b=True: Lin(ini, n, k, b)  # noqa: E731

@@ -172,3 +172,13 @@ def cfg_euler(x, out, B, seq, first, dt, cfg):
 def step_end(stop_logits, patch, patches, stop, ctr, lens, B, min_len, max_steps):
     _lib.call("oumu_step_end", _p(stop_logits), _p(patch), _p(patches), _p(stop), _p(ctr), _p(lens), B, min_len,
               max_steps, _stream())
+
+
+def gemm(x, w, y, bias=None):
+    """y[M][N] = bf16(x[M][K] . w[N][K]^T (+ bias)) on the tensor cores; x and y may be row-strided views."""
+    M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K or x.stride(1) != 1 or y.stride(1) != 1 or not w.is_contiguous() or tuple(y.shape) != (M, N):
+        raise ValueError("gemm: x [M][K] and y [M][N] with unit column stride, w [N][K] contiguous")
+    _lib.call("oumu_gemm", _p(x), x.stride(0), _p(w), _p(y), y.stride(0), _p(bias), M, N, K, _stream())
+    return y
