@@ -215,7 +215,8 @@ __device__ __forceinline__ void merge_segment(const Params &P, const float *F, i
     sync();
     const int cf = cta_of(Sg, W, Gc), cl = cta_of(Eg - 1, W, Gc);
     if (old != cl - cf) return;
-    // last contributor: merge every CTA's partial of this segment (all loads of a record issued together)
+    // last contributor: merge every CTA's partial of this segment in one online pass (the records of four
+    // contributors are loaded together: one round trip to L2 per four)
     float M2[NH], L2[NH];
 #pragma unroll
     for (int k = 0; k < NH; k++) {
@@ -225,14 +226,6 @@ __device__ __forceinline__ void merge_segment(const Params &P, const float *F, i
         for (int e = 0; e < DL; e++) o[k][e] = 0.f;
     }
 #pragma unroll 4
-    for (int cc = cf; cc <= cl; cc++) {
-        const long ac = static_cast<long>(cc) * W / Gc;
-        const float *rc = P.part + (static_cast<long>(cc) * 2 + ((cc == cf && ac < Sg) ? 1 : 0)) * C::PART_FLOATS;
-#pragma unroll
-        for (int k = 0; k < NH; k++)
-            if (hb + k * HS < GMAX) M2[k] = fmaxf(M2[k], __ldcg(rc + hb + k * HS));
-    }
-#pragma unroll 2
     for (int cc = cf; cc <= cl; cc++) {
         const long ac = static_cast<long>(cc) * W / Gc;
         const float *rc = P.part + (static_cast<long>(cc) * 2 + ((cc == cf && ac < Sg) ? 1 : 0)) * C::PART_FLOATS;
@@ -253,11 +246,14 @@ __device__ __forceinline__ void merge_segment(const Params &P, const float *F, i
         }
 #pragma unroll
         for (int k = 0; k < NH; k++) {
-            if (hb + k * HS >= GMAX) continue;
-            const float wc = mc[k] == -INFINITY ? 0.f : fast_exp2(mc[k] - M2[k]);
-            L2[k] += wc * lc[k];
+            if (hb + k * HS >= GMAX || mc[k] == -INFINITY) continue;
+            const float mn = fmaxf(M2[k], mc[k]);
+            const float wa = M2[k] == -INFINITY ? 0.f : fast_exp2(M2[k] - mn);
+            const float wc = fast_exp2(mc[k] - mn);
+            M2[k] = mn;
+            L2[k] = L2[k] * wa + lc[k] * wc;
 #pragma unroll
-            for (int e = 0; e < DL; e++) o[k][e] += wc * oc[k][e];
+            for (int e = 0; e < DL; e++) o[k][e] = o[k][e] * wa + oc[k][e] * wc;
         }
     }
     store(L2);
