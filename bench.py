@@ -33,6 +33,25 @@ WORKLOAD = ("config 2: decode attention, 28 layers x 64 takes per GPU, 16 q / 2 
             "of 4096, per-take lengths U[330,4096], one query per take per layer, one CUDA graph per step")
 
 
+# The JSON line is the only thing on standard output: everything else (NCCL's banner, library messages) is sent to
+# standard error by pointing file descriptor 1 there, and the line is written to the original standard output.
+_STDOUT_FD = None
+
+
+def quiet_stdout():
+    global _STDOUT_FD
+    if _STDOUT_FD is None:
+        sys.stdout.flush()
+        _STDOUT_FD = os.dup(1)
+        os.dup2(2, 1)
+
+
+def emit(line):
+    sys.stdout.flush()
+    data = (json.dumps(line) + "\n").encode()
+    os.write(_STDOUT_FD if _STDOUT_FD is not None else 1, data)
+
+
 def take_lengths(rank):
     from oumu_b200 import synth
     return synth.uniform_int(synth.config_seed(1) + 1000 * rank, TAKES, LEN_LO, LEN_HI)
@@ -204,7 +223,7 @@ def reference_arm(args, rank, world):
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference implements this path only as CUDA kernels; its CPU form is the oracle port",
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -292,6 +311,7 @@ def main():
     ap.add_argument("--step-takes", type=int, default=STEP_TAKES, help="takes per GPU of the decoding-step leg")
     ap.add_argument("--step-steps", type=int, default=30, help="timed decoding steps of the decoding-step leg")
     args = ap.parse_args()
+    quiet_stdout()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -457,7 +477,7 @@ def main():
             "device_error": errword,
             "patches_per_s": step,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     del graph
     if world > 1:
         dist.barrier()
