@@ -164,6 +164,16 @@ int oumu_attn_full(const void *qkv, void *out, int rows, int seq, int causal, in
 int oumu_kv_replicate(void *cache, int B, int nk, int maxlen, int hd, int T, oumu_stream_t stream);
 
 /*
+ * Causal prefill of one prompt with the KV epilogue, one launch: out = the causal attention of qkv's T rows (as
+ * oumu_attn_full(qkv, out, T, T, 1, ...)), and the prompt's k and v (already rotated) written into positions [0, T) of
+ * every one of the `slots` take slots of kc and vc ([slots][nk][maxlen][hd]); positions >= T are not touched.
+ * Replaces, per layer, kv_write into slot 0 + attn_full (src/model.rs:553-567) and the later kv_replicate into slots
+ * 1..B-1 (src/model.rs:705-717). T > 16 (the tensor-core path), T <= maxlen; caches bit-exact.
+ */
+int oumu_attn_prefill_kv(const void *qkv, void *out, void *kc, void *vc, int T, int slots, int nq, int nk, int hd,
+                         int maxlen, float scale, oumu_stream_t stream);
+
+/*
  * Device-side error word of this library on the current device: 0 when no kernel recorded an error (a bounded
  * wait that ran out, a length outside [1, maxlen]). Synchronises the device. reset != 0 clears it.
  */

@@ -156,6 +156,18 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *m, 
         : "memory");
 }
 
+// Shared -> global tensor store of a 3-D box at (x, y, z) (coordinates >= 0; rows past the map's extent are not
+// written), tracked by this thread's bulk groups.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *m, uint32_t src, int x, int y, int z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(m)),
+                 "r"(src), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until this thread's committed bulk copies have finished reading their shared-memory sources.
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
 // ---------------------------------------------------------------------------------------------------------
 // Warp-level tensor-core fragments (m16n8k16, bf16 in, fp32 accumulate)
 // ---------------------------------------------------------------------------------------------------------

@@ -141,6 +141,29 @@ int make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, u
     return OUMU_OK;
 }
 
+// 3-D bf16 map over the layer caches [slots][nk][maxlen][hd] restricted to the first T positions: dims
+// {hd, T, slots * nk}, box {64, box_rows, 1}, 128-byte swizzle; boxes reaching past position T are clipped.
+int make_map_cache(CUtensorMap *m, const void *base, int hd, int T, int planes, int maxlen, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) {
+        std::snprintf(g_last_cuda, sizeof(g_last_cuda), "cuTensorMapEncodeTiled unavailable");
+        return OUMU_ERR_CUDA;
+    }
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(hd), static_cast<cuuint64_t>(T), static_cast<cuuint64_t>(planes)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(hd) * 2, static_cast<cuuint64_t>(maxlen) * hd * 2};
+    cuuint32_t box[3] = {64, box_rows, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        std::snprintf(g_last_cuda, sizeof(g_last_cuda), "cuTensorMapEncodeTiled (cache) failed (%d)",
+                      static_cast<int>(r));
+        return OUMU_ERR_CUDA;
+    }
+    return OUMU_OK;
+}
+
 uint16_t f2b_host(float x) {  // round-to-nearest-even, NaN -> 0x7fc0 (src/gpu.rs:72-78)
     if (std::isnan(x)) return 0x7fc0;
     uint32_t u;
@@ -219,18 +242,27 @@ int launch_small(const void *qkv, void *out, int rows, int seq, int causal, int 
     return OUMU_OK;
 }
 
+// Prefill attention; with kc/vc (slots > 0) also the KV epilogue into every slot's first `seq` positions.
 template <int HD>
 int launch_prefill(const void *qkv, void *out, int rows, int seq, int causal, int nq, int nk, float scale,
-                   cudaStream_t st) {
-    CUtensorMap tm;
+                   cudaStream_t st, void *kc = nullptr, void *vc = nullptr, int slots = 0, int maxlen = 0) {
+    CUtensorMap tm, tkc, tvc;
+    std::memset(&tkc, 0, sizeof(tkc));
+    std::memset(&tvc, 0, sizeof(tvc));
     const uint64_t width = static_cast<uint64_t>(nq + 2 * nk) * HD;
     int rc = make_map(&tm, qkv, width, rows, width * 2, 64, pf::BM);
     if (rc) return rc;
+    if (slots > 0) {
+        rc = make_map_cache(&tkc, kc, HD, seq, slots * nk, maxlen, pf::BN);
+        if (rc) return rc;
+        rc = make_map_cache(&tvc, vc, HD, seq, slots * nk, maxlen, pf::BN);
+        if (rc) return rc;
+    }
     const int nseq = rows / seq;
     if (nseq > 65535 || nq > 65535) return OUMU_ERR_UNSUPPORTED;
     dim3 grid((seq + pf::BM - 1) / pf::BM, nq, nseq);
     pf::k_attn_prefill<HD><<<grid, pf::NTHREADS, pf::Cfg<HD>::SMEM, st>>>(
-        tm, static_cast<bf16 *>(out), seq, causal, nq, nk, scale * 1.4426950408889634f);
+        tm, static_cast<bf16 *>(out), seq, causal, nq, nk, scale * 1.4426950408889634f, tkc, tvc, slots);
     OUMU_CK(cudaGetLastError());
     return OUMU_OK;
 }
@@ -553,6 +585,22 @@ int oumu_attn_full(const void *qkv, void *out, int rows, int seq, int causal, in
     }
     return hd == 128 ? launch_prefill<128>(qkv, out, rows, seq, causal, nq, nk, scale, st)
                      : launch_prefill<64>(qkv, out, rows, seq, causal, nq, nk, scale, st);
+}
+
+int oumu_attn_prefill_kv(const void *qkv, void *out, void *kc, void *vc, int T, int slots, int nq, int nk, int hd,
+                         int maxlen, float scale, oumu_stream_t stream) {
+    if (!qkv || !out || !kc || !vc || T < 1 || slots < 1 || nq < 1 || nk < 1 || nq % nk || maxlen < T ||
+        !(scale > 0.f))
+        return OUMU_ERR_INVALID;
+    if (!head_dim_ok(hd)) return OUMU_ERR_UNSUPPORTED;
+    if (T <= fs::ROWS) return OUMU_ERR_UNSUPPORTED;  // the tensor-core path only (prompts longer than 16)
+    if (!aligned16(qkv) || !aligned16(out) || !aligned16(kc) || !aligned16(vc)) return OUMU_ERR_INVALID;
+    int sms = 0;
+    int rc = current_device(&sms);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    return hd == 128 ? launch_prefill<128>(qkv, out, T, T, 1, nq, nk, scale, st, kc, vc, slots, maxlen)
+                     : launch_prefill<64>(qkv, out, T, T, 1, nq, nk, scale, st, kc, vc, slots, maxlen);
 }
 
 int oumu_kv_replicate(void *cache, int B, int nk, int maxlen, int hd, int T, oumu_stream_t stream) {

@@ -14,6 +14,11 @@
 //               when the max has grown by more than 2^8 (lazy rescaling: until then the stale max is kept, which
 //               changes no result because O and the sum use the same one). The halves of the sum meet once, at the
 //               end, and each warpgroup writes bf16(O * (1 / sum)) for its 64 columns.
+// KV epilogue (oumu_attn_prefill_kv, slots > 0): the prompt's k and v also go into every take's cache slot, with TMA
+// tensor stores from the 128-byte-swizzled tiles in shared memory through a map whose extent is the prompt length (rows
+// past it are never written). The CTA of query tile qt copies key tile ntiles - 1 - qt, the G q heads of a kv head
+// splitting the slots: the longest CTAs (late query tiles) copy early key tiles right after loading them, under the
+// rest of their math; the shortest ones load and copy the late tiles after their own few tiles.
 // All waits are bounded (mbar_wait); on a timeout the kernel records the error and winds down.
 #pragma once
 #include "common.cuh"
@@ -42,12 +47,13 @@ struct Cfg {
 
 // barrier slots (8 bytes each) inside the barrier area
 enum { B_Q = 0, B_KVF0 = 1, B_KVF1 = 2, B_KVE0 = 3, B_KVE1 = 4, B_SFULL = 5, B_SFREE = 6, B_PFULL = 7, B_ODONE = 8,
-       B_TMEM = 12, B_ABORT = 13 };
+       B_COPY = 9, B_TMEM = 12, B_ABORT = 13 };
 
 template <int HD>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_attn_prefill(const __grid_constant__ CUtensorMap tqkv, bf16 *__restrict__ out, int seq, int causal, int nq,
-                   int nk, float sl2) {
+                   int nk, float sl2, const __grid_constant__ CUtensorMap tkc,
+                   const __grid_constant__ CUtensorMap tvc, int slots) {
     using C = Cfg<HD>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_s = smem_u32(smem_raw);
@@ -76,6 +82,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         mbar_init(bar(B_SFREE), 8);
         mbar_init(bar(B_PFULL), 8);
         mbar_init(bar(B_ODONE), 1);
+        mbar_init(bar(B_COPY), 1);
         *abort_flag = 0;
         mbar_fence_init();
     }
@@ -90,30 +97,80 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     if (warp == 0) {
         // ------------------------------ TMA producer ------------------------------
+        // Lane 0 issues the loads; the KV epilogue's stores are spread over the warp's 32 lanes (one thread keeps
+        // only a few bulk copies in flight). Every wait is taken by the whole warp, so control flow stays uniform.
         if (lane == 0) {
             tma_prefetch_desc(&tqkv);
             mbar_expect_tx(bar(B_Q), C::NBOX * BOX);
 #pragma unroll
             for (int bx = 0; bx < C::NBOX; bx++)
                 tma_load_2d(sm_s + C::Q_OFF + bx * BOX, &tqkv, bar(B_Q), h * HD + bx * 64, row0 + q0);
-            for (int j = 0; j < ntiles; j++) {
-                const int st = j & 1;
-                if (j >= 2 && !mbar_wait(bar(B_KVE0 + st), ((j >> 1) - 1) & 1)) {
-                    *abort_flag = 1;
-                    break;
-                }
-                if (*abort_flag) break;
-                const uint32_t fb = bar(B_KVF0 + st);
+        }
+        // this CTA's share of the KV epilogue: key tile cj of kv head kh into slots [s0, s1)
+        const int cj = ntiles_all - 1 - qt, g = h % G;
+        const int per = slots > 0 ? (slots + G - 1) / G : 0, s0 = g * per, s1 = min(slots, s0 + per);
+        const bool copy = slots > 0 && causal && s0 < s1;
+        auto load_kv = [&](int stg, int tj, uint32_t fb) {
+            if (lane == 0) {
                 mbar_expect_tx(fb, 2 * C::NBOX * BOX);
 #pragma unroll
                 for (int bx = 0; bx < C::NBOX; bx++) {
-                    tma_load_2d(sm_s + C::K_OFF + (st * C::NBOX + bx) * BOX, &tqkv, fb, (nq + kh) * HD + bx * 64,
-                                row0 + j * BN);
-                    tma_load_2d(sm_s + C::V_OFF + (st * C::NBOX + bx) * BOX, &tqkv, fb,
-                                (nq + nk + kh) * HD + bx * 64, row0 + j * BN);
+                    tma_load_2d(sm_s + C::K_OFF + (stg * C::NBOX + bx) * BOX, &tqkv, fb, (nq + kh) * HD + bx * 64,
+                                row0 + tj * BN);
+                    tma_load_2d(sm_s + C::V_OFF + (stg * C::NBOX + bx) * BOX, &tqkv, fb,
+                                (nq + nk + kh) * HD + bx * 64, row0 + tj * BN);
+                }
+            }
+            __syncwarp();
+        };
+        auto store_tile = [&](int stg) {  // (slot, box, K or V) items over the lanes
+            const int items = (s1 - s0) * C::NBOX * 2;
+            for (int it = lane; it < items; it += 32) {
+                const int kv = it & 1, bx = (it >> 1) % C::NBOX, sl = s0 + (it >> 1) / C::NBOX;
+                tma_store_3d(kv ? &tvc : &tkc, sm_s + (kv ? C::V_OFF : C::K_OFF) + (stg * C::NBOX + bx) * BOX,
+                             bx * 64, cj * BN, sl * nk + kh);
+            }
+            bulk_commit();
+        };
+        bool ok = true, stored = false;
+        for (int j = 0; j < ntiles; j++) {
+            const int st = j & 1;
+            if (j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KVE0 + st), ((j >> 1) - 1) & 1));
+            ok = __all_sync(0xffffffffu, ok && *abort_flag == 0);
+            if (!ok) break;
+            if (copy && stored && j == cj + 2) bulk_wait_read();  // the copy of tile cj has read this stage
+            load_kv(st, j, bar(B_KVF0 + st));
+            if (copy && j == cj + 1) {  // tile cj, requested one step ago, goes out as soon as it has landed
+                ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KVF0 + (cj & 1)), (cj >> 1) & 1));
+                if (!ok) break;
+                store_tile(cj & 1);
+                stored = true;
+            }
+        }
+        if (ok && copy && !stored) {
+            if (cj < ntiles) {
+                // the CTA's last tile: still in its stage
+                ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KVF0 + (cj & 1)), (cj >> 1) & 1));
+                if (ok) {
+                    store_tile(cj & 1);
+                    stored = true;
+                }
+            } else {
+                // a tile this CTA does not attend to: into stage 0 once its last use there (tile jl) is done
+                const int jl = (ntiles - 1) & ~1;
+                ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KVE0), (jl >> 1) & 1));
+                if (ok) {
+                    load_kv(0, cj, bar(B_COPY));
+                    ok = __all_sync(0xffffffffu, mbar_wait(bar(B_COPY), 0));
+                    if (ok) {
+                        store_tile(0);
+                        stored = true;
+                    }
                 }
             }
         }
+        if (stored) bulk_wait_read();  // shared memory stays in place until every store has read it
+        if (!ok && lane == 0) *abort_flag = 1;
         __syncwarp();  // the warp reaches the final CTA barrier converged
     } else if (warp == 1) {
         // ------------------------------ MMA issuer ------------------------------

@@ -182,3 +182,10 @@ def gemm(x, w, y, bias=None):
         raise ValueError("gemm: x [M][K] and y [M][N] with unit column stride, w [N][K] contiguous")
     _lib.call("oumu_gemm", _p(x), x.stride(0), _p(w), _p(y), y.stride(0), _p(bias), M, N, K, _stream())
     return y
+
+
+def attn_prefill_kv(qkv, out, kc, vc, T, slots, nq, nk, hd, maxlen, scale):
+    """Causal prefill of one prompt + its k/v into every take slot, one launch (oumu_attn_prefill_kv): replaces
+    kv_write + attn_full (src/model.rs:553-567) and kv_replicate (src/model.rs:705-717)."""
+    _lib.call("oumu_attn_prefill_kv", _p(qkv), _p(out), _p(kc), _p(vc), T, slots, nq, nk, hd, maxlen, float(scale),
+              _stream())

@@ -9,6 +9,7 @@ CASE: decode (config 2: 64 takes, slots of 4096, lengths U[330,4096]; per layer)
       decode1 (config 1: one take, 512 of 4096 positions)
       prefill (config 3: T = 1024 causal, 16 q / 2 kv heads, hd 128; per layer)
       replicate (config 3: the prompt KV of one layer, K and V, into 64 slots of 4096)
+      prefill_kv (config 3 per layer in one launch: prefill + k/v into all 64 slots; and the separate launches)
       locdit (config 4: 512 sequences x 12 tokens, 16 heads, hd 64)
       locdit_ref (the reference's DiT shape: 512 sequences x 11 tokens, 16 q / 2 kv heads, hd 128)
 Prints one JSON line: mean milliseconds per launch (CUDA events on the launching stream, after warm-up) and the
@@ -164,6 +165,29 @@ def case_replicate(args, impl, B=64, maxlen=4096, T=1024):
     return dict(ms=ms, bytes=nbytes, GBps=nbytes / ms / 1e6)
 
 
+def case_prefill_kv(args, B=64, maxlen=4096, T=1024):
+    """Config 3 per layer in one launch: causal prefill + the prompt's k/v into all B slots (oumu_attn_prefill_kv);
+    against it, the separate launches (kv_write, attention, replication of K and V)."""
+    layers = args.layers
+    qkv = [rnd((T, (NQ + 2 * NK) * HD), 300 + l) for l in range(layers)]
+    out = torch.zeros((T, NQ * HD), dtype=torch.bfloat16, device="cuda")
+    kc, vc = rnd((B, NK, maxlen, HD), 401), rnd((B, NK, maxlen, HD), 402)
+    flops = 4 * NQ * HD * T * (T + 1) // 2
+
+    def fused(i):
+        ops.attn_prefill_kv(qkv[i % layers], out, kc, vc, T, B, NQ, NK, HD, maxlen, HD ** -0.5)
+
+    def separate(i):
+        ops.kv_write(qkv[i % layers], kc, vc, None, 1, T, NQ, NK, HD, maxlen)
+        ops.attn_full(qkv[i % layers], out, T, T, 1, NQ, NK, HD, HD ** -0.5)
+        ops.kv_replicate(kc, B, NK, maxlen, HD, T)
+        ops.kv_replicate(vc, B, NK, maxlen, HD, T)
+    ms = timed(fused, args.reps, args.warmup)
+    ms_sep = timed(separate, args.reps, args.warmup)
+    return dict(ms=ms, ms_separate=ms_sep, flops=flops, TFLOPs=flops / ms / 1e9,
+                kv_bytes_written=2 * B * NK * T * HD * 2)
+
+
 def case_small(args, impl, nseq, seq, nq, nk, hd):
     rows, W = nseq * seq, (nq + 2 * nk) * hd
     layers = max(args.layers, 8)  # rotate inputs so consecutive calls do not hit L2
@@ -207,6 +231,8 @@ def main():
         r = case_prefill(args, args.impl)
     elif c == "replicate":
         r = case_replicate(args, args.impl)
+    elif c == "prefill_kv":
+        r = case_prefill_kv(args)
     elif c == "locdit":
         r = case_small(args, args.impl, 512, 12, 16, 16, 64)
     elif c == "locdit_ref":
