@@ -1,8 +1,9 @@
 // Attention inside many short independent sequences (seq <= 16): the LocDiT passes (11 or 12 tokens, all takes x
 // both CFG branches in one launch) and the local encoder (5 tokens).
 //
-// One warp per (sequence, q head) unit, persistent over units. The warp stages its q, k and v rows (16-byte
-// cp.async, 128-byte-swizzled rows, padding rows zeroed) in its own shared-memory slice, then on tensor cores:
+// k_attn_small (one q head per kv head): one warp per (sequence, q head) unit, persistent over units. The warp stages
+// its q, k and v rows (16-byte cp.async, 128-byte-swizzled rows, padding rows zeroed) in its own shared-memory slice,
+// then on tensor cores:
 //   S[16 x 16] = Q[16 x hd] . K^T          (mma.sync m16n8k16, fp32 accumulate)
 //   row softmax in fp32 (exp2 with the scale folded), masked keys (>= seq, or causal) -> 0
 //   O[16 x hd] = P . V                       (P split as bf16 hi + lo, so the weights keep ~16 mantissa bits)
@@ -135,6 +136,140 @@ __global__ void __launch_bounds__(WARPS * 32) k_attn_small(const bf16 *__restric
             }
         }
         __syncwarp();
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// k_attn_small_grp (grouped-query attention, G = nq / nk > 1, G * seq <= 128): one CTA per (sequence, kv head).
+// The G q heads of the group are stacked as one tall Q (row g * seq + r = head g, query r; padded to MT 16-row
+// tiles); the CTA stages K and V once and the whole stack (every byte read from memory once per group, not once
+// per q head), then warp t computes Q tile t: S = Q_t K^T, masked row softmax, O = P V, out = bf16(O * (1 / sum)) —
+// the arithmetic of k_attn_small row for row.
+// ------------------------------------------------------------------------------------------------------------
+constexpr int MAXM = 128;  // stacked q rows at most: MT <= 8 warps
+
+template <int HD>
+struct GCfg {
+    static constexpr int NBOX = HD / 64;
+    static constexpr int TILE_BYTES = NBOX * ROWS * 128;  // one 16-row matrix, 128-B swizzled rows per 64-wide box
+    static constexpr int smem_bytes(int mt) { return (2 + mt) * TILE_BYTES; }  // K, V, the Q tiles
+};
+
+template <int HD>
+__global__ void __launch_bounds__(MAXM / ROWS * 32) k_attn_small_grp(const bf16 *__restrict__ qkv,
+                                                                     bf16 *__restrict__ out, int seq, int causal,
+                                                                     int nq, int nk, float sl2) {
+    using C = GCfg<HD>;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nthr = blockDim.x;
+    const uint32_t ks_ = smem_u32(smem), vs = ks_ + C::TILE_BYTES, qs0 = vs + C::TILE_BYTES;
+    const int stride = (nq + 2 * nk) * HD, G = nq / nk;
+    const int CPR = HD / 8;  // 16-byte chunks per row
+    const int M = G * seq, MT = nthr / 32;
+    const int n = blockIdx.x / nk, kh = blockIdx.x % nk;
+    const bf16 *base = qkv + static_cast<long>(n) * seq * stride;
+    const int r4 = lane >> 2, c2 = (lane & 3) * 2, mi = lane >> 3;
+
+    // ---- stage k, v (16 rows, zero past seq) and the stacked q rows (MT * 16, zero past M) ----
+    const int kvitems = 2 * ROWS * CPR;
+    for (int i = threadIdx.x; i < kvitems + MT * ROWS * CPR; i += nthr) {
+        if (i < kvitems) {
+            const int mat = i / (ROWS * CPR), rem = i % (ROWS * CPR), r = rem / CPR, ch = rem % CPR;
+            const uint32_t dst = (mat == 0 ? ks_ : vs) + (ch >> 3) * (ROWS * 128) + sw128(r, ch & 7);
+            if (r < seq) {
+                cp_async16(dst, base + static_cast<long>(r) * stride + (mat == 0 ? nq + kh : nq + nk + kh) * HD +
+                                    ch * 8);
+            } else {
+                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0) : "memory");
+            }
+        } else {
+            const int j = i - kvitems, m = j / CPR, ch = j % CPR;
+            const uint32_t dst = qs0 + (m >> 4) * C::TILE_BYTES + (ch >> 3) * (ROWS * 128) + sw128(m & 15, ch & 7);
+            if (m < M) {
+                const int g = m / seq, r = m - g * seq;
+                cp_async16(dst, base + static_cast<long>(r) * stride + (kh * G + g) * HD + ch * 8);
+            } else {
+                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0) : "memory");
+            }
+        }
+    }
+    cp_async_wait_all();
+    __syncthreads();
+
+    const uint32_t qs = qs0 + warp * C::TILE_BYTES;
+    // ---- S = Q_t K^T ----
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ks++) {
+        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+        const uint32_t boff = (ks >> 2) * (ROWS * 128);
+        ldsm_x4(qs + boff + sw128((mi & 1) * 8 + (lane & 7), 2 * (ks & 3) + (mi >> 1)), a0, a1, a2, a3);
+        ldsm_x4(ks_ + boff + sw128((mi >> 1) * 8 + (lane & 7), 2 * (ks & 3) + (mi & 1)), b0, b1, b2, b3);
+        mma_bf16_16816(s[0], a0, a1, a2, a3, b0, b1);
+        mma_bf16_16816(s[1], a0, a1, a2, a3, b2, b3);
+    }
+    // ---- masked row softmax (stacked rows warp*16 + r4 and + 8) ----
+    const int m0 = warp * 16 + r4, m1 = m0 + 8;
+    const int q0 = m0 % seq, q1 = m1 % seq;  // query positions within the sequence
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int qr = (e >> 1) ? q1 : q0, key = nt * 8 + c2 + (e & 1);
+            const bool ok = key < seq && (!causal || key <= qr);
+            s[nt][e] = ok ? s[nt][e] * sl2 : -INFINITY;
+            mx[e >> 1] = fmaxf(mx[e >> 1], s[nt][e]);
+        }
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+        mx[k] = fmaxf(mx[k], __shfl_xor_sync(0xffffffffu, mx[k], 1));
+        mx[k] = fmaxf(mx[k], __shfl_xor_sync(0xffffffffu, mx[k], 2));
+        if (mx[k] == -INFINITY) mx[k] = 0.f;  // padding rows only
+    }
+    float sum[2] = {0.f, 0.f};
+#pragma unroll
+    for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            s[nt][e] = fast_exp2(s[nt][e] - mx[e >> 1]);
+            sum[e >> 1] += s[nt][e];
+        }
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+        sum[k] += __shfl_xor_sync(0xffffffffu, sum[k], 1);
+        sum[k] += __shfl_xor_sync(0xffffffffu, sum[k], 2);
+    }
+    uint32_t ph[4], pl[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int nt = k >> 1, e = (k & 1) * 2;
+        const float x0 = s[nt][e], x1 = s[nt][e + 1];
+        ph[k] = pack_bf16x2(x0, x1);
+        const float2 hv = unpack_bf16x2(ph[k]);
+        pl[k] = pack_bf16x2(x0 - hv.x, x1 - hv.y);
+    }
+    // ---- O = P V; stacked row m is query m % seq of q head kh * G + m / seq ----
+    const float inv0 = 1.f / sum[0], inv1 = 1.f / sum[1];
+    const bool st0 = m0 < M, st1 = m1 < M;
+    bf16 *o0 = out + (static_cast<long>(n) * seq + q0) * nq * HD + (kh * G + m0 / seq) * HD;
+    bf16 *o1 = out + (static_cast<long>(n) * seq + q1) * nq * HD + (kh * G + m1 / seq) * HD;
+#pragma unroll
+    for (int dt = 0; dt < HD / 8; dt += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int ch = dt + (mi >> 1);
+        ldsm_x4_t(vs + (ch >> 3) * (ROWS * 128) + sw128((mi & 1) * 8 + (lane & 7), ch & 7), b0, b1, b2, b3);
+        float o[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        mma_bf16_16816(o[0], ph[0], ph[1], ph[2], ph[3], b0, b1);
+        mma_bf16_16816(o[0], pl[0], pl[1], pl[2], pl[3], b0, b1);
+        mma_bf16_16816(o[1], ph[0], ph[1], ph[2], ph[3], b2, b3);
+        mma_bf16_16816(o[1], pl[0], pl[1], pl[2], pl[3], b2, b3);
+#pragma unroll
+        for (int tt = 0; tt < 2; tt++) {
+            const int d = (dt + tt) * 8 + c2;
+            if (st0) *reinterpret_cast<uint32_t *>(o0 + d) = pack_bf16x2(o[tt][0] * inv0, o[tt][1] * inv0);
+            if (st1) *reinterpret_cast<uint32_t *>(o1 + d) = pack_bf16x2(o[tt][2] * inv1, o[tt][3] * inv1);
+        }
     }
 }
 

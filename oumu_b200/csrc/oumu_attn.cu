@@ -89,6 +89,10 @@ int current_device(int *sms) {
                                      pf::Cfg<128>::SMEM));
         OUMU_CK(cudaFuncSetAttribute(pf::k_attn_prefill<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      pf::Cfg<64>::SMEM));
+        OUMU_CK(cudaFuncSetAttribute(fs::k_attn_small_grp<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     fs::GCfg<128>::smem_bytes(fs::MAXM / fs::ROWS)));
+        OUMU_CK(cudaFuncSetAttribute(fs::k_attn_small_grp<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     fs::GCfg<64>::smem_bytes(fs::MAXM / fs::ROWS)));
         OUMU_CK(cudaFuncSetAttribute(gm::k_gemm<32, kGemmStages32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kSmemMax));
         OUMU_CK(cudaFuncSetAttribute(gm::k_gemm<64, kGemmStages64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -230,6 +234,17 @@ int launch_decode(const void *qkv, const void *kc, const void *vc, void *out, vo
 template <int HD>
 int launch_small(const void *qkv, void *out, int rows, int seq, int causal, int nq, int nk, float scale, int sms,
                  cudaStream_t st) {
+    const int G = nq / nk;
+    if (G > 1 && G * seq <= fs::MAXM) {  // grouped heads: one CTA per (sequence, kv head), K/V staged once
+        const long ctas = static_cast<long>(rows / seq) * nk;
+        if (ctas > 0x7fffffffL) return OUMU_ERR_UNSUPPORTED;
+        const int mt = (G * seq + fs::ROWS - 1) / fs::ROWS;
+        fs::k_attn_small_grp<HD><<<static_cast<unsigned>(ctas), mt * 32, fs::GCfg<HD>::smem_bytes(mt), st>>>(
+            static_cast<const bf16 *>(qkv), static_cast<bf16 *>(out), seq, causal, nq, nk,
+            scale * 1.4426950408889634f);
+        OUMU_CK(cudaGetLastError());
+        return OUMU_OK;
+    }
     const long units = static_cast<long>(rows / seq) * nq;
     long grid = (units + fs::WARPS - 1) / fs::WARPS;
     const long cap = static_cast<long>(sms) * 8;
