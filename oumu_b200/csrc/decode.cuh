@@ -119,13 +119,15 @@ __device__ __forceinline__ int cta_of(long t, long W, int G) {
 
 // Merge of one segment end, run by NT threads (32: the merger warp; NCW*32: the consumer warps together).
 // Thread i owns hd columns [lane*DL, lane*DL + DL) of heads i/32 + k*NT/32, so shared-memory reads, partial records
-// and outputs are contiguous across each warp. F holds the NCW warp states (m[8], l[8], o[8][HD] each). Writes the
-// segment's output when the whole segment is in this CTA; otherwise this CTA's partial, and if it is the last
-// contributor (atomic counter) merges every contributor's partial and writes the output.
-template <int HD, int NT>
+// and outputs are contiguous across each warp. F holds the NCW warp states (m[8], l[8], o[8][HD] each); `release`
+// runs as soon as they are read (the merger hands the flush buffer back to the consumers there, before its global
+// writes and the cross-CTA round trips). Writes the segment's output when the whole segment is in this CTA;
+// otherwise this CTA's partial, and if it is the last contributor (atomic counter) merges every contributor's
+// partial and writes the output.
+template <int HD, int NT, class Release>
 __device__ __forceinline__ void merge_segment(const Params &P, const float *F, int s, int kh, long Sg, long Eg,
                                               long ta, long tb, long W, int Gc, int c, int slot, int tid,
-                                              volatile int *bcast) {
+                                              volatile int *bcast, Release release) {
     using C = Cfg<HD>;
     constexpr int DL = HD / 32;         // hd columns per thread: 4 (hd 128) or 2 (hd 64)
     constexpr int HS = NT / 32;                 // head stride between a thread's heads
@@ -169,6 +171,7 @@ __device__ __forceinline__ void merge_segment(const Params &P, const float *F, i
             }
         }
     }
+    release();
     bf16 *dst = P.out + static_cast<long>(s) * P.nq * HD + kh * G * HD + d0;
     auto store = [&](const float (&l)[NH]) {
 #pragma unroll
@@ -261,20 +264,29 @@ __device__ __forceinline__ void merge_segment(const Params &P, const float *F, i
 }
 
 // Fused form: the newest position's k and v, handled by the consumer warp that owns the segment's last tile.
-// newest_load fetches the raw rows (lanes < KG: 8 rope pairs of k each; the next VC lanes: 16 bytes of v each);
-// newest_store rotates k (same arithmetic as the rope kernel, kernels/voxcpm.cu:109-114), writes k and v into the
-// cache slot and the rotated k back into qkv (in place, like rope), and patches row r of the shared-memory tile
-// that TMA loaded before the position was written.
+// newest_load fetches the raw rows (lanes < KG: 8 rope pairs of k each, with their rotary table entries; the next
+// VC lanes: 16 bytes of v each), all before the tile is awaited; newest_store rotates k (same arithmetic as the
+// rope kernel, kernels/voxcpm.cu:109-114), writes k and v into the cache slot and the rotated k back into qkv (in
+// place, like rope), and patches row r of the shared-memory tile that TMA loaded before the position was written.
 template <int HD>
 struct Newest {
     static constexpr int HALF = HD / 2, KG = HALF / 8, VC = HD / 8;
     uint4 a, b;
-    __device__ __forceinline__ void load(const Params &P, int s, int kh, int lane) {
+    float4 c0, c1, s0, s1;
+    __device__ __forceinline__ void load(const Params &P, int s, int kh, int p, int lane) {
         const bf16 *row = P.qkv + static_cast<long>(s) * (P.nq + 2 * P.nk) * HD;
         if (lane < KG) {
             const bf16 *k = row + (P.nq + kh) * HD + lane * 8;
             a = *reinterpret_cast<const uint4 *>(k);
             b = *reinterpret_cast<const uint4 *>(k + HALF);
+            if (P.cos_t) {
+                const float4 *cp = reinterpret_cast<const float4 *>(P.cos_t + static_cast<long>(p) * HALF + lane * 8);
+                const float4 *sp = reinterpret_cast<const float4 *>(P.sin_t + static_cast<long>(p) * HALF + lane * 8);
+                c0 = cp[0];
+                c1 = cp[1];
+                s0 = sp[0];
+                s1 = sp[1];
+            }
         } else if (lane < KG + VC) {
             a = reinterpret_cast<const uint4 *>(row + (P.nq + P.nk + kh) * HD)[lane - KG];
         }
@@ -285,9 +297,6 @@ struct Newest {
         if (lane < KG) {
             const int i = lane * 8;
             if (P.cos_t) {
-                const float4 *cp = reinterpret_cast<const float4 *>(P.cos_t + static_cast<long>(p) * HALF + i);
-                const float4 *sp = reinterpret_cast<const float4 *>(P.sin_t + static_cast<long>(p) * HALF + i);
-                const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
                 const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
                 const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
                 const bf16 *x = reinterpret_cast<const bf16 *>(&a);
@@ -474,9 +483,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
                 const long Sg = pre[it.s] + static_cast<long>(it.kh) * it.T;
                 merge_segment<HD, 32>(P, flush + b * NCW * C::PART_FLOATS, it.s, it.kh, Sg, Sg + it.T, ta, tb, W,
-                                      Gc, c, nflush == 0 ? 0 : 1, lane, misc + 2);
+                                      Gc, c, nflush == 0 ? 0 : 1, lane, misc + 2, [&] {
+                                          __syncwarp();
+                                          if (lane == 0) mbar_arrive(bar_fempty + 8 * b);
+                                      });
                 __syncwarp();
-                if (lane == 0) mbar_arrive(bar_fempty + 8 * b);
                 nflush++;
             }
             it.next(Ls, nk);
@@ -519,7 +530,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const uint32_t use = ntile >> 1;
             const bool newest = FUSED && it.j == it.T - 1;
             Newest<HD> nw;
-            if (newest) nw.load(P, it.s, it.kh, lane);  // in flight while the tile is awaited
+            if (newest) nw.load(P, it.s, it.kh, it.L - 1, lane);  // in flight while the tile is awaited
             bool ok = misc[0] == 0;
             if (ok && !mbar_wait(bar_full + 8 * st, use & 1u)) {
                 misc[0] = 1;
@@ -648,7 +659,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 bar_consumers();
                 const long Sg = pre[it.s] + static_cast<long>(it.kh) * it.T;
                 merge_segment<HD, NCW * 32>(P, Fb, it.s, it.kh, Sg, Sg + it.T, ta, tb, W, Gc, c,
-                                            nflush == 0 ? 0 : 1, threadIdx.x, misc + 1);
+                                            nflush == 0 ? 0 : 1, threadIdx.x, misc + 1, [] {});
             } else {
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar_ffull + 8 * (nflush % NFB));
