@@ -157,6 +157,16 @@ int oumu_attn_full(const void *qkv, void *out, int rows, int seq, int causal, in
                    oumu_stream_t stream);
 
 /*
+ * Rope + attention of one layer of Engine::full in one launch, for the small sequences of the DiT and the local
+ * encoder: out = oumu_attn_full of qkv with q and k rotated at positions r % seq (the tables of oumu_rope, at least
+ * seq rows), bit-identical to oumu_rope followed by oumu_attn_full. qkv itself is not modified.
+ * Replaces the rope + attn_full launches of src/model.rs:541-567 (kernels/voxcpm.cu:100-115, 262-297).
+ * Supported: seq <= 16, nq / nk >= 2, (nq / nk) * seq <= 128, hd in {64, 128}; other shapes OUMU_ERR_UNSUPPORTED.
+ */
+int oumu_attn_full_rope(const void *qkv, void *out, const float *cos_t, const float *sin_t, int rows, int seq,
+                        int causal, int nq, int nk, int hd, float scale, oumu_stream_t stream);
+
+/*
  * Replicate slot 0 of a per-layer cache [B][nk][maxlen][hd] into slots 1..B-1 for positions < T.
  * Replaces kv_replicate (kernels/voxcpm.cu:407-413), launched per K and V cache at src/model.rs:705-717.
  * Bit-exact copy; reads slot 0 once and writes the other B-1 slots.

@@ -30,6 +30,7 @@ SIGNATURES = {
     "oumu_attn_decode_static": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P]),
     "oumu_attn_decode_step": (_I, [_P, _P, _P, _P, _P, _Z, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P]),
     "oumu_attn_full": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _F, _P]),
+    "oumu_attn_full_rope": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P]),
     "oumu_kv_replicate": (_I, [_P, _I, _I, _I, _I, _I, _P]),
     "oumu_attn_prefill_kv": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P]),
     "oumu_device_error": (_I, [_I]),

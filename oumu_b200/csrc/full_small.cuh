@@ -145,6 +145,9 @@ __global__ void __launch_bounds__(WARPS * 32) k_attn_small(const bf16 *__restric
 // tiles); the CTA stages K and V once and the whole stack (every byte read from memory once per group, not once
 // per q head), then warp t computes Q tile t: S = Q_t K^T, masked row softmax, O = P V, out = bf16(O * (1 / sum)) —
 // the arithmetic of k_attn_small row for row.
+// ROPE: q and k are rotated while they are staged (position r of the sequence, the arithmetic of k_rope:
+// x1' = bf16(x1*c - x2*s), x2' = bf16(x2*c + x1*s)), so one launch replaces rope + attention of Engine::full
+// (src/model.rs:541-567) with the same result; qkv itself is left unrotated.
 // ------------------------------------------------------------------------------------------------------------
 constexpr int MAXM = 128;  // stacked q rows at most: MT <= 8 warps
 
@@ -155,10 +158,41 @@ struct GCfg {
     static constexpr int smem_bytes(int mt) { return (2 + mt) * TILE_BYTES; }  // K, V, the Q tiles
 };
 
+// Stage one rotated chunk pair of a q or k row: chunks p and p + HD/16 (elements [8p, 8p+8) and the same + HD/2)
+// rotated with the table row `pos`, stored into a 16-row swizzled matrix at row r.
 template <int HD>
+__device__ __forceinline__ void stage_rope_pair(uint32_t mat, int r, int p, const bf16 *row, const float *cos_t,
+                                                const float *sin_t, int pos) {
+    constexpr int HALF = HD / 2, HP = HD / 16;
+    const uint4 u1 = *reinterpret_cast<const uint4 *>(row + p * 8);
+    const uint4 u2 = *reinterpret_cast<const uint4 *>(row + HALF + p * 8);
+    const float4 *cp = reinterpret_cast<const float4 *>(cos_t + static_cast<long>(pos) * HALF + p * 8);
+    const float4 *sp = reinterpret_cast<const float4 *>(sin_t + static_cast<long>(pos) * HALF + p * 8);
+    const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+    const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const bf16 *a = reinterpret_cast<const bf16 *>(&u1);
+    const bf16 *b = reinterpret_cast<const bf16 *>(&u2);
+    uint4 o1, o2;
+    bf16 *oa = reinterpret_cast<bf16 *>(&o1);
+    bf16 *ob = reinterpret_cast<bf16 *>(&o2);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float x1 = bf2f(a[j]), x2 = bf2f(b[j]);
+        oa[j] = f2bf(x1 * c[j] - x2 * sn[j]);
+        ob[j] = f2bf(x2 * c[j] + x1 * sn[j]);
+    }
+    const int q = p + HP;  // the partner chunk
+    st_shared_v4(mat + (p >> 3) * (ROWS * 128) + sw128(r, p & 7), o1);
+    st_shared_v4(mat + (q >> 3) * (ROWS * 128) + sw128(r, q & 7), o2);
+}
+
+template <int HD, bool ROPE>
 __global__ void __launch_bounds__(MAXM / ROWS * 32) k_attn_small_grp(const bf16 *__restrict__ qkv,
                                                                      bf16 *__restrict__ out, int seq, int causal,
-                                                                     int nq, int nk, float sl2) {
+                                                                     int nq, int nk, float sl2,
+                                                                     const float *__restrict__ cos_t,
+                                                                     const float *__restrict__ sin_t) {
     using C = GCfg<HD>;
     extern __shared__ __align__(1024) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nthr = blockDim.x;
@@ -171,25 +205,61 @@ __global__ void __launch_bounds__(MAXM / ROWS * 32) k_attn_small_grp(const bf16 
     const int r4 = lane >> 2, c2 = (lane & 3) * 2, mi = lane >> 3;
 
     // ---- stage k, v (16 rows, zero past seq) and the stacked q rows (MT * 16, zero past M) ----
-    const int kvitems = 2 * ROWS * CPR;
-    for (int i = threadIdx.x; i < kvitems + MT * ROWS * CPR; i += nthr) {
-        if (i < kvitems) {
-            const int mat = i / (ROWS * CPR), rem = i % (ROWS * CPR), r = rem / CPR, ch = rem % CPR;
-            const uint32_t dst = (mat == 0 ? ks_ : vs) + (ch >> 3) * (ROWS * 128) + sw128(r, ch & 7);
-            if (r < seq) {
-                cp_async16(dst, base + static_cast<long>(r) * stride + (mat == 0 ? nq + kh : nq + nk + kh) * HD +
-                                    ch * 8);
+    if constexpr (ROPE) {
+        // v by 16-byte chunks (cp.async); k and q by rotated chunk pairs through registers
+        constexpr int HP = HD / 16;
+        const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+        const int vitems = ROWS * CPR, kitems = ROWS * HP;
+        for (int i = threadIdx.x; i < vitems + kitems + MT * ROWS * HP; i += nthr) {
+            if (i < vitems) {
+                const int r = i / CPR, ch = i % CPR;
+                const uint32_t dst = vs + (ch >> 3) * (ROWS * 128) + sw128(r, ch & 7);
+                if (r < seq) cp_async16(dst, base + static_cast<long>(r) * stride + (nq + nk + kh) * HD + ch * 8);
+                else st_shared_v4(dst, zero);
+            } else if (i < vitems + kitems) {
+                const int j = i - vitems, r = j / HP, p = j % HP;
+                if (r < seq) {
+                    stage_rope_pair<HD>(ks_, r, p, base + static_cast<long>(r) * stride + (nq + kh) * HD, cos_t,
+                                        sin_t, r);
+                } else {
+                    st_shared_v4(ks_ + (p >> 3) * (ROWS * 128) + sw128(r, p & 7), zero);
+                    st_shared_v4(ks_ + ((p + HP) >> 3) * (ROWS * 128) + sw128(r, (p + HP) & 7), zero);
+                }
             } else {
-                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0) : "memory");
+                const int j = i - vitems - kitems, m = j / HP, p = j % HP;
+                const uint32_t mat = qs0 + (m >> 4) * C::TILE_BYTES;
+                if (m < M) {
+                    const int g = m / seq, r = m - g * seq;
+                    stage_rope_pair<HD>(mat, m & 15, p, base + static_cast<long>(r) * stride + (kh * G + g) * HD,
+                                        cos_t, sin_t, r);
+                } else {
+                    st_shared_v4(mat + (p >> 3) * (ROWS * 128) + sw128(m & 15, p & 7), zero);
+                    st_shared_v4(mat + ((p + HP) >> 3) * (ROWS * 128) + sw128(m & 15, (p + HP) & 7), zero);
+                }
             }
-        } else {
-            const int j = i - kvitems, m = j / CPR, ch = j % CPR;
-            const uint32_t dst = qs0 + (m >> 4) * C::TILE_BYTES + (ch >> 3) * (ROWS * 128) + sw128(m & 15, ch & 7);
-            if (m < M) {
-                const int g = m / seq, r = m - g * seq;
-                cp_async16(dst, base + static_cast<long>(r) * stride + (kh * G + g) * HD + ch * 8);
+        }
+    } else {
+        const int kvitems = 2 * ROWS * CPR;
+        for (int i = threadIdx.x; i < kvitems + MT * ROWS * CPR; i += nthr) {
+            if (i < kvitems) {
+                const int mat = i / (ROWS * CPR), rem = i % (ROWS * CPR), r = rem / CPR, ch = rem % CPR;
+                const uint32_t dst = (mat == 0 ? ks_ : vs) + (ch >> 3) * (ROWS * 128) + sw128(r, ch & 7);
+                if (r < seq) {
+                    cp_async16(dst, base + static_cast<long>(r) * stride + (mat == 0 ? nq + kh : nq + nk + kh) * HD +
+                                        ch * 8);
+                } else {
+                    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0) : "memory");
+                }
             } else {
-                asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0) : "memory");
+                const int j = i - kvitems, m = j / CPR, ch = j % CPR;
+                const uint32_t dst =
+                    qs0 + (m >> 4) * C::TILE_BYTES + (ch >> 3) * (ROWS * 128) + sw128(m & 15, ch & 7);
+                if (m < M) {
+                    const int g = m / seq, r = m - g * seq;
+                    cp_async16(dst, base + static_cast<long>(r) * stride + (kh * G + g) * HD + ch * 8);
+                } else {
+                    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0) : "memory");
+                }
             }
         }
     }

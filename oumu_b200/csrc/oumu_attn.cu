@@ -89,9 +89,13 @@ int current_device(int *sms) {
                                      pf::Cfg<128>::SMEM));
         OUMU_CK(cudaFuncSetAttribute(pf::k_attn_prefill<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      pf::Cfg<64>::SMEM));
-        OUMU_CK(cudaFuncSetAttribute(fs::k_attn_small_grp<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        OUMU_CK(cudaFuncSetAttribute(fs::k_attn_small_grp<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      fs::GCfg<128>::smem_bytes(fs::MAXM / fs::ROWS)));
-        OUMU_CK(cudaFuncSetAttribute(fs::k_attn_small_grp<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        OUMU_CK(cudaFuncSetAttribute(fs::k_attn_small_grp<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     fs::GCfg<128>::smem_bytes(fs::MAXM / fs::ROWS)));
+        OUMU_CK(cudaFuncSetAttribute(fs::k_attn_small_grp<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     fs::GCfg<64>::smem_bytes(fs::MAXM / fs::ROWS)));
+        OUMU_CK(cudaFuncSetAttribute(fs::k_attn_small_grp<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      fs::GCfg<64>::smem_bytes(fs::MAXM / fs::ROWS)));
         OUMU_CK(cudaFuncSetAttribute(gm::k_gemm<32, kGemmStages32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kSmemMax));
@@ -233,18 +237,20 @@ int launch_decode(const void *qkv, const void *kc, const void *vc, void *out, vo
 
 template <int HD>
 int launch_small(const void *qkv, void *out, int rows, int seq, int causal, int nq, int nk, float scale, int sms,
-                 cudaStream_t st) {
+                 cudaStream_t st, const float *cos_t = nullptr, const float *sin_t = nullptr) {
     const int G = nq / nk;
     if (G > 1 && G * seq <= fs::MAXM) {  // grouped heads: one CTA per (sequence, kv head), K/V staged once
         const long ctas = static_cast<long>(rows / seq) * nk;
         if (ctas > 0x7fffffffL) return OUMU_ERR_UNSUPPORTED;
         const int mt = (G * seq + fs::ROWS - 1) / fs::ROWS;
-        fs::k_attn_small_grp<HD><<<static_cast<unsigned>(ctas), mt * 32, fs::GCfg<HD>::smem_bytes(mt), st>>>(
+        auto kern = cos_t ? fs::k_attn_small_grp<HD, true> : fs::k_attn_small_grp<HD, false>;
+        kern<<<static_cast<unsigned>(ctas), mt * 32, fs::GCfg<HD>::smem_bytes(mt), st>>>(
             static_cast<const bf16 *>(qkv), static_cast<bf16 *>(out), seq, causal, nq, nk,
-            scale * 1.4426950408889634f);
+            scale * 1.4426950408889634f, cos_t, sin_t);
         OUMU_CK(cudaGetLastError());
         return OUMU_OK;
     }
+    if (cos_t) return OUMU_ERR_UNSUPPORTED;  // rope fused only into the grouped kernel
     const long units = static_cast<long>(rows / seq) * nq;
     long grid = (units + fs::WARPS - 1) / fs::WARPS;
     const long cap = static_cast<long>(sms) * 8;
@@ -600,6 +606,23 @@ int oumu_attn_full(const void *qkv, void *out, int rows, int seq, int causal, in
     }
     return hd == 128 ? launch_prefill<128>(qkv, out, rows, seq, causal, nq, nk, scale, st)
                      : launch_prefill<64>(qkv, out, rows, seq, causal, nq, nk, scale, st);
+}
+
+int oumu_attn_full_rope(const void *qkv, void *out, const float *cos_t, const float *sin_t, int rows, int seq,
+                        int causal, int nq, int nk, int hd, float scale, oumu_stream_t stream) {
+    if (!qkv || !out || !cos_t || !sin_t || rows < 0 || seq < 1 || nq < 1 || nk < 1 || nq % nk || !(scale > 0.f))
+        return OUMU_ERR_INVALID;
+    if (rows % seq) return OUMU_ERR_INVALID;
+    if (!head_dim_ok(hd)) return OUMU_ERR_UNSUPPORTED;
+    if (seq > fs::ROWS || nq / nk < 2 || (nq / nk) * seq > fs::MAXM) return OUMU_ERR_UNSUPPORTED;
+    if (!aligned16(qkv) || !aligned16(out) || !aligned16(cos_t) || !aligned16(sin_t)) return OUMU_ERR_INVALID;
+    if (rows == 0) return OUMU_OK;
+    int sms = 0;
+    int rc = current_device(&sms);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    return hd == 128 ? launch_small<128>(qkv, out, rows, seq, causal, nq, nk, scale, sms, st, cos_t, sin_t)
+                     : launch_small<64>(qkv, out, rows, seq, causal, nq, nk, scale, sms, st, cos_t, sin_t);
 }
 
 int oumu_attn_prefill_kv(const void *qkv, void *out, void *kc, void *vc, int T, int slots, int nq, int nk, int hd,

@@ -122,9 +122,26 @@ def step_tf_attention(qkv, kc, vc, att, workspace, cos_t, sin_t, ctr, lens, B, n
     attn_decode(qkv, kc, vc, att, workspace, pos, lens, B, nq, nk, hd, maxlen, 1.0 / hd ** 0.5)
 
 
+def attn_full_rope(qkv, att, cos_t, sin_t, rows, seq, causal, nq, nk, hd, scale):
+    """Rope at positions r % seq + attention in one launch (small grouped sequences); qkv is left unrotated."""
+    _lib.call("oumu_attn_full_rope", _p(qkv), _p(att), _p(cos_t), _p(sin_t), rows, seq, int(bool(causal)), nq, nk,
+              hd, float(scale), _stream())
+    return att
+
+
+def rope_fusable(seq, nq, nk):
+    """Shapes oumu_attn_full_rope takes (the grouped small-sequence kernel)."""
+    return seq <= 16 and nq // nk >= 2 and (nq // nk) * seq <= 128
+
+
 def full_attention(qkv, att, rows, seq, causal, nq, nk, hd, maxlen=0, cos_t=None, sin_t=None, kc=None, vc=None):
     """The attention part of one layer of Engine::full (src/model.rs:541-567): rope over positions r % seq,
-    kv_write of every row into slot 0 when caches are given, then attention inside the sequences."""
+    kv_write of every row into slot 0 when caches are given, then attention inside the sequences. Small grouped
+    sequences without caches (the DiT, the local encoder) take the one-launch rope + attention, which leaves qkv
+    unrotated; otherwise q and k are rotated in place first."""
+    if cos_t is not None and kc is None and rope_fusable(seq, nq, nk):
+        attn_full_rope(qkv, att, cos_t, sin_t, rows, seq, causal, nq, nk, hd, 1.0 / hd ** 0.5)
+        return
     if cos_t is not None:
         rope(qkv, cos_t, sin_t, None, rows, seq, nq, nk, hd)
     if kc is not None:
