@@ -119,21 +119,27 @@ class ClockSampler:
         except Exception as e:  # no NVML: the line says so
             self.err = str(e)
 
-    def _run(self):
+    def sample(self):
         nv = self.nv
+        try:
+            self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            for bit, name in self.REASONS.items():
+                if r & bit:
+                    self.reasons.add(name)
+        except Exception:
+            pass
+
+    def _run(self):
         while not self.stop:
-            try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
-                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                for bit, name in self.REASONS.items():
-                    if r & bit:
-                        self.reasons.add(name)
-            except Exception:
-                pass
+            self.sample()
             time.sleep(0.01)
 
     def __enter__(self):
+        # one sample on entry and one on exit in the caller's thread (a short timed region can end before the
+        # sampling thread gets scheduled), the thread's in between
         if self.ok:
+            self.sample()
             self.stop = False
             self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
@@ -141,6 +147,7 @@ class ClockSampler:
 
     def __exit__(self, *a):
         if self.ok:
+            self.sample()
             self.stop = True
             self.t.join()
 
@@ -395,6 +402,7 @@ def main():
         for _ in range(args.steps):
             graph.replay()
         e1.record()
+        clocks.sample()  # the replays are queued: the GPU is busy with them now
         torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1))
     barrier()
