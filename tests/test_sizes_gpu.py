@@ -85,6 +85,43 @@ def test_decode_shapes_and_lengths(cuda, nq, nk, hd):
     gc.assert_close(u16(att), oracle_decode(qkv, kc, vc, lens, B, maxlen, nq, nk, hd), f"{nq}/{nk}/{hd}")
 
 
+@pytest.mark.parametrize("B,maxlen,fused", [(256, 192, False), (1024, 64, False), (1024, 64, True)])
+def test_decode_many_takes(cuda, B, maxlen, fused):
+    # the reference's MAX_SLOTS (256, src/model.rs:25) and the engine's 1024 takes per GPU: every CTA range then
+    # crosses many short segments (lengths 1 .. maxlen)
+    lens = [int(v) for v in synth.uniform_int(1234 + B, B, 1, maxlen)]
+    qkv, kc, vc, ln = decode_case(B, lens, maxlen, seed=40)
+    if not fused:
+        att, _ = run_decode(qkv, kc, vc, ln, B, maxlen)
+        gc.assert_close(u16(att), oracle_decode(qkv, kc, vc, lens, B, maxlen), f"{B} takes")
+        return
+    # fused (no rope): the newest k/v go into each take's slot at lens - 1, then attention over [0, lens)
+    qkv_h, kc_h, vc_h = u16(qkv), u16(kc), u16(vc)
+    att = torch.zeros((B, NQ * HD), dtype=torch.bfloat16, device="cuda")
+    ws = ops.decode_workspace(B, NQ, NK, HD, maxlen)
+    ops.step_tf_attention(qkv, kc, vc, att, ws, None, None, None, ln, B, NQ, NK, HD, maxlen, rope_on=False)
+    torch.cuda.synchronize()
+    for t, L in enumerate(lens):
+        kcs, vcs = np.ascontiguousarray(kc_h[t:t + 1]), np.ascontiguousarray(vc_h[t:t + 1])
+        cpu.kv_write(np.ascontiguousarray(qkv_h[t:t + 1]), kcs, vcs, L - 1, 1, 1, NQ, NK, HD, maxlen)
+        kc_h[t], vc_h[t] = kcs[0], vcs[0]
+    assert np.array_equal(u16(kc), kc_h) and np.array_equal(u16(vc), vc_h)
+    ref = cpu.attn_decode(qkv_h, kc_h, vc_h, None, np.asarray(lens, np.int32), B, NQ, NK, HD, maxlen, HD ** -0.5)
+    gc.assert_close(u16(att), ref, f"{B} takes fused")
+
+
+def test_decode_rejects_takes_past_shared_memory(cuda):
+    # the per-take tile prefix lives in shared memory: far more takes than the engine's 1024 are refused with
+    # OUMU_ERR_UNSUPPORTED before any launch
+    from oumu_b200 import _lib
+    B, maxlen = 4096, 32
+    qkv, kc, vc, ln = decode_case(B, [1] * B, maxlen, seed=41)
+    att = torch.zeros((B, NQ * HD), dtype=torch.bfloat16, device="cuda")
+    ws = ops.decode_workspace(B, NQ, NK, HD, maxlen)
+    with pytest.raises(_lib.OumuError):
+        ops.attn_decode(qkv, kc, vc, att, ws, None, ln, B, NQ, NK, HD, maxlen, HD ** -0.5)
+
+
 def test_decode_shared_position_and_max_length(cuda):
     # the reference's form: one shared *pos for every take; and the longest KV the reference accepts (65536)
     B, maxlen = 2, 65536
