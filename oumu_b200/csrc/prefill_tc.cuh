@@ -5,12 +5,14 @@
 //   warp 0      TMA producer: Q tile once, then K/V tiles of 128 positions into a 2-stage ring
 //   warp 1      TMEM allocator and the single MMA-issuing thread:
 //                 S  = Q . K_j^T      (M=128 queries, N=128 keys, K=hd; A and B K-major, 128-B swizzle)
-//                 O += P_j . V_j      (M=128, N=hd, K=128 keys; A = P from shared memory, B = V MN-major)
+//                 O += P_j . V_j      (M=128, N=hd, K=128 keys; A = P from tensor memory, B = V MN-major)
 //   warps 2..9  softmax, two warpgroups: warpgroup g owns columns [64g, 64g+64) of every row (thread = row of its
 //               TMEM lane quarter). Each thread reads its whole S row from TMEM for the row max (the two halves of a
 //               row compute the same value, so nothing is exchanged), exponentiates its own 64 columns, keeps its
-//               half of the row sum, writes its half of P_j to shared memory as two bf16 matrices hi + lo (so the
-//               weights keep ~16 mantissa bits; O += P_hi.V + P_lo.V) and rescales its half of the O row in TMEM
+//               half of the row sum, writes its half of P_j into TMEM as two bf16 matrices hi + lo (so the weights
+//               keep ~16 mantissa bits; O += P_hi.V + P_lo.V), in one of two P buffers: P_{j+1} is written while
+//               P_j.V runs, and a buffer is reused once the P.V two tiles back has read it. It rescales its half of
+//               the O row in TMEM
 //               when the max has grown by more than 2^8 (lazy rescaling: until then the stale max is kept, which
 //               changes no result because O and the sum use the same one). The halves of the sum meet once, at the
 //               end, and each warpgroup writes bf16(O * (1 / sum)) for its 64 columns.
@@ -37,17 +39,17 @@ struct Cfg {
     static constexpr int Q_OFF = 0;
     static constexpr int K_OFF = Q_OFF + NBOX * BOX;         // 2 stages
     static constexpr int V_OFF = K_OFF + 2 * NBOX * BOX;     // 2 stages
-    static constexpr int P_OFF = V_OFF + 2 * NBOX * BOX;     // P hi: 2 boxes (keys 0-63, 64-127), then P lo
-    static constexpr int PLO_OFF = P_OFF + 2 * BOX;
-    static constexpr int BAR_OFF = PLO_OFF + 2 * BOX;
-    static constexpr int SMEM = BAR_OFF + 128 + 1024;        // + alignment slack
-    static constexpr uint32_t TMEM_COLS = 256;               // S: 128 columns, O: hd columns
-    static constexpr uint32_t O_COL = 128;
+    static constexpr int BAR_OFF = V_OFF + 2 * NBOX * BOX;
+    static constexpr int LX_OFF = BAR_OFF + 128;             // the two halves of the row sums, 2 x 128 floats
+    static constexpr int SMEM = LX_OFF + 1024 + 1024;        // + alignment slack
+    // TMEM: S (128 columns), two P buffers (hi: 64 columns of bf16 pairs, lo: 64), O (hd columns)
+    static constexpr uint32_t TMEM_COLS = 512;
+    static constexpr uint32_t P_COL = 128, O_COL = 384;
 };
 
 // barrier slots (8 bytes each) inside the barrier area
 enum { B_Q = 0, B_KVF0 = 1, B_KVF1 = 2, B_KVE0 = 3, B_KVE1 = 4, B_SFULL = 5, B_SFREE = 6, B_PFULL = 7, B_ODONE = 8,
-       B_COPY = 9, B_TMEM = 12, B_ABORT = 13 };
+       B_COPY = 9, B_PDONE0 = 10, B_PDONE1 = 11, B_TMEM = 12, B_ABORT = 13 };
 
 template <int HD>
 __global__ void __launch_bounds__(NTHREADS, 1)
@@ -83,6 +85,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         mbar_init(bar(B_PFULL), 8);
         mbar_init(bar(B_ODONE), 1);
         mbar_init(bar(B_COPY), 1);
+        mbar_init(bar(B_PDONE0), 1);
+        mbar_init(bar(B_PDONE1), 1);
         *abort_flag = 0;
         mbar_fence_init();
     }
@@ -209,14 +213,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t vbase = sm_s + C::V_OFF + (j & 1) * C::NBOX * BOX;
+                const uint32_t tP = tmem + C::P_COL + (j & 1) * 128;  // hi at +0, lo at +64 (16 keys per 8 columns)
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; kk++) {
-                    const uint32_t poff = (kk >> 2) * BOX + (kk & 3) * 32;
                     const uint64_t b = smem_desc_sw128(vbase + kk * 2048, BOX, 1024);
-                    tc_mma_ss(tO, smem_desc_sw128(sm_s + C::P_OFF + poff, 16, 1024), b, idO, (j > 0 || kk > 0) ? 1u : 0u);
-                    tc_mma_ss(tO, smem_desc_sw128(sm_s + C::PLO_OFF + poff, 16, 1024), b, idO, 1u);
+                    tc_mma_ts(tO, tP + kk * 8, b, idO, (j > 0 || kk > 0) ? 1u : 0u);
+                    tc_mma_ts(tO, tP + 64 + kk * 8, b, idO, 1u);
                 }
                 tc_commit(bar(B_ODONE));
+                tc_commit(bar(B_PDONE0 + (j & 1)));
                 tc_commit(bar(B_KVE0 + (j & 1)));
             }
             if (!ok) *abort_flag = 1;
@@ -289,12 +294,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
             l = l * alpha + rs;
-            // P_j may overwrite P_{j-1} and O may be rescaled once PV_{j-1} has completed
-            if (j > 0) {
+            // P_j goes into buffer j & 1 once PV_{j-2} has read it; O may be rescaled once PV_{j-1} has completed
+            if (j >= 2) {
+                ok = __all_sync(0xffffffffu, mbar_wait(bar(B_PDONE0 + (j & 1)), ((j >> 1) - 1) & 1));
+                if (!ok) break;
+            }
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
                 ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE), (j - 1) & 1));
                 if (!ok) break;
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.f)) {
+                {
 #pragma unroll
                     for (int c = 0; c < OH; c += 32) {
                         uint32_t orow[32];
@@ -307,31 +316,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     tc_wait_st();
                 }
             }
-            // this half of P row r -> shared memory (box wg), K-major 128-byte swizzle: 8 chunks of 8 keys
+            // this half of P row r (keys cb .. cb + 63) -> TMEM buffer j & 1 as bf16 pairs: hi (the bf16 of p) in
+            // columns [32wg, 32wg + 32), lo (the rest) in [64 + 32wg, ...); sr[k] takes the k-th hi pair in place
+            uint32_t lw[32];
 #pragma unroll
-            for (int cc = 0; cc < 8; cc++) {
-                uint32_t hi[4], lo[4];
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const float p0 = __uint_as_float(sr[cc * 8 + 2 * k]);
-                    const float p1 = __uint_as_float(sr[cc * 8 + 2 * k + 1]);
-                    hi[k] = pack_bf16x2(p0, p1);
-                    const float2 hv = unpack_bf16x2(hi[k]);
-                    lo[k] = pack_bf16x2(p0 - hv.x, p1 - hv.y);
-                }
-                const uint32_t off = wg * BOX + sw128(r, cc);
-                *reinterpret_cast<uint4 *>(sm + C::P_OFF + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4 *>(sm + C::PLO_OFF + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            for (int k = 0; k < 32; k++) {
+                const float p0 = __uint_as_float(sr[2 * k]), p1 = __uint_as_float(sr[2 * k + 1]);
+                const uint32_t hw = pack_bf16x2(p0, p1);
+                const float2 hv = unpack_bf16x2(hw);
+                lw[k] = pack_bf16x2(p0 - hv.x, p1 - hv.y);
+                sr[k] = hw;
             }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            const uint32_t tPb = tmem + lane_off + C::P_COL + (j & 1) * 128;
+            tmem_st32(tPb + wg * 32, sr);
+            tmem_st32(tPb + 64 + wg * 32, lw);
+            tc_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(B_PFULL));
         }
         if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE), (ntiles - 1) & 1));
         if (!ok) *abort_flag = 1;
-        // the two halves of each row sum meet in the (now idle) P buffer
-        float *lx = reinterpret_cast<float *>(sm + C::P_OFF);
+        // the two halves of each row sum meet in shared memory
+        float *lx = reinterpret_cast<float *>(sm + C::LX_OFF);
         lx[wg * BM + r] = l;
         asm volatile("bar.sync 1, 256;" ::: "memory");
         const float ltot = l + lx[(1 - wg) * BM + r];
