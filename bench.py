@@ -244,7 +244,7 @@ STEP_WORKLOAD = ("config 5: random-init VoxCPM2-shaped decoding step per GPU, on
                  "SwiGLU 6144) -> FSQ -> residual LM (8 layers); KV slots of 4096, lengths U[330, 4096)")
 
 
-def patches_leg(args, dev, rank, max_over_ranks, sum_over_ranks, barrier):
+def patches_leg(args, dev, rank, max_over_ranks, sum_over_ranks, barrier, world=1):
     """Config 5: the whole decoding step (oumu_b200.engine) for --step-takes takes per GPU, as one CUDA graph;
     patches/s over all ranks, device-resident and end to end (the step's noise uploaded from pinned host memory,
     the new patch and the stop flags read back and waited for every step, as Engine::decode reads `stop`,
@@ -290,6 +290,13 @@ def patches_leg(args, dev, rank, max_over_ranks, sum_over_ranks, barrier):
 
     e2e_ms = timed(e2e_step)
     patches = sum_over_ranks(B * K)
+    # after the timed region: every rank's finished patches and stop steps to every rank, the sharded decode's one
+    # collective (once per text)
+    gathered = None
+    if world > 1:
+        gp, gs = engine.gather_patches(e.patches, e.stop)
+        torch.cuda.synchronize()
+        gathered = {"takes": int(gp.shape[0]), "bytes_per_rank": int(e.patches.numel() * 2 + e.stop.numel() * 4)}
     kv = 2 * 2 * 128 * 2 * (len(e.base.layers) + len(e.res.layers)) * int(sum(int(v) + W + K // 2 for v in lens))
     wbytes = e.step_weight_bytes()
     flops = e.step_flops()
@@ -305,6 +312,7 @@ def patches_leg(args, dev, rank, max_over_ranks, sum_over_ranks, barrier):
                 "ms_per_step": round(e2e_ms / K, 4),
                 "path": "pinned host noise -> device, graph replay, patch + stop flags -> pinned host, host sync"},
         "gpu_launches_per_step": launches,
+        "patches_gathered": gathered,
     }
 
 def main():
@@ -488,7 +496,7 @@ def main():
     errword = ops.device_error()
     barrier()
 
-    step = None if args.no_step else patches_leg(args, dev, rank, max_over_ranks, sum_over_ranks, barrier)
+    step = None if args.no_step else patches_leg(args, dev, rank, max_over_ranks, sum_over_ranks, barrier, world)
 
     cpu_base = None
     if world == 1 and not args.no_cpu:

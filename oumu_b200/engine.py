@@ -56,6 +56,26 @@ def schedule(n):
     return out
 
 
+def gather_patches(patches, stop, group=None):
+    """Every rank's finished patches [B][max_steps][PATCH] and stop steps [B] in rank order (rank r's takes at
+    [r*B, (r+1)*B)): the one collective of a decode sharded over GPUs by takes, once per text after the last step (the
+    reference keeps every take on one GPU and reads them back there, src/model.rs:785-796). torch.distributed
+    all_gather over the process group's backend (NCCL for device tensors, gloo for host tensors; the tensors cross as
+    their bytes); without a process group, the tensors themselves."""
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()):
+        return patches, stop
+    world = dist.get_world_size(group)
+
+    def allgather(t):
+        wire = t.contiguous().view(torch.uint8)  # bytes: every backend carries them, whatever the element type
+        parts = [torch.empty_like(wire) for _ in range(world)]
+        dist.all_gather(parts, wire, group=group)
+        return torch.cat(parts).view(t.dtype)
+
+    return allgather(patches), allgather(stop)
+
+
 class _Init:
     def __init__(self, seed, device):
         self.g = torch.Generator(device=device)

@@ -52,3 +52,51 @@ def test_single_process_reduce_is_identity():
     sys.path.insert(0, ROOT)
     import bench
     assert bench.rank_reduce(5.0, "max") == 5.0
+
+
+def _gather_worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, ROOT)
+    from oumu_b200 import engine
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    try:
+        B, S = 3, 5
+        patches = (torch.arange(B * S * engine.PATCH, dtype=torch.float32).view(B, S, engine.PATCH) + 1000 * rank
+                   ).to(torch.bfloat16)
+        stop = torch.tensor([10 * rank + k for k in range(B)], dtype=torch.int32)
+        gp, gs = engine.gather_patches(patches, stop)
+        q.put((rank, gp.view(torch.int16).numpy().copy(), gs.numpy().copy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_ranks_gather_finished_patches():
+    # the sharded decode's one collective: every rank ends with all takes' patches and stop steps in rank order
+    import numpy as np
+    import torch
+    sys.path.insert(0, ROOT)
+    from oumu_b200 import engine
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 30500 + (os.getpid() % 1000)
+    procs = [ctx.Process(target=_gather_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r = q.get(timeout=120)
+        res[r[0]] = r
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    B, S = 3, 5
+    want = torch.cat([(torch.arange(B * S * engine.PATCH, dtype=torch.float32).view(B, S, engine.PATCH) + 1000 * r
+                       ).to(torch.bfloat16) for r in range(2)]).view(torch.int16).numpy()
+    for r in range(2):
+        assert np.array_equal(res[r][1], want)
+        assert res[r][2].tolist() == [0, 1, 2, 10, 11, 12]
+    # one process, no group: the tensors come back as they are
+    p1, s1 = engine.gather_patches(torch.zeros(2, 3, engine.PATCH, dtype=torch.bfloat16), torch.zeros(2, dtype=torch.int32))
+    assert p1.shape == (2, 3, engine.PATCH) and s1.shape == (2,)
