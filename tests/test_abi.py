@@ -69,6 +69,29 @@ def test_invalid_arguments_are_rejected_on_the_host(lib):
     assert lib.oumu_attn_decode_workspace(4, 16, 3, 128, 4096) == 0
 
 
+def test_invalid_arguments_of_the_fused_and_step_entry_points(lib):
+    P = ctypes.c_void_p(16 * 1024)  # never dereferenced: validation fails first
+    # rope + small attention: no rotary tables; sequences longer than 16; one q head per kv head; a stacked group
+    # of more than 128 rows (32 q heads x 5 tokens)
+    assert lib.oumu_attn_full_rope(P, P, None, P, 22, 11, 0, 16, 2, 128, 0.1, None) == _lib.ERR_INVALID
+    assert lib.oumu_attn_full_rope(P, P, P, P, 34, 17, 0, 16, 2, 128, 0.1, None) == _lib.ERR_UNSUPPORTED
+    assert lib.oumu_attn_full_rope(P, P, P, P, 22, 11, 0, 16, 16, 128, 0.1, None) == _lib.ERR_UNSUPPORTED
+    assert lib.oumu_attn_full_rope(P, P, P, P, 10, 5, 0, 64, 2, 128, 0.1, None) == _lib.ERR_UNSUPPORTED
+    # prefill with the KV epilogue: prompt longer than the slot; no slots; prompts of 16 or fewer (small path)
+    assert lib.oumu_attn_prefill_kv(P, P, P, P, 65, 4, 16, 2, 128, 64, 0.1, None) == _lib.ERR_INVALID
+    assert lib.oumu_attn_prefill_kv(P, P, P, P, 32, 0, 16, 2, 128, 64, 0.1, None) == _lib.ERR_INVALID
+    assert lib.oumu_attn_prefill_kv(P, P, P, P, 16, 4, 16, 2, 128, 64, 0.1, None) == _lib.ERR_UNSUPPORTED
+    # step glue: RMS norm width, SwiGLU width, FSQ scale, build_seq shape, cfg_euler token window, step_end steps
+    assert lib.oumu_rmsnorm(P, None, P, P, 4, 1536, 1e-5, None) == _lib.ERR_UNSUPPORTED
+    assert lib.oumu_silu_mul(P, P, 4, 12, None) == _lib.ERR_INVALID
+    assert lib.oumu_pointwise(P, 64, 1, 0.0, None) == _lib.ERR_INVALID
+    assert lib.oumu_build_seq(P, P, P, P, P, 6, 2, 11, 1024, None) == _lib.ERR_INVALID  # rows != 2 B for the DiT
+    assert lib.oumu_cfg_euler(P, P, 4, 11, 8, 0.1, 2.0, None) == _lib.ERR_INVALID
+    assert lib.oumu_step_end(P, P, P, P, P, P, 4, 2, 0, None) == _lib.ERR_INVALID
+    # projection GEMM: K not a multiple of its 64-element tile
+    assert lib.oumu_gemm(P, 100, P, P, 128, None, 4, 128, 100, None) == _lib.ERR_INVALID
+
+
 @pytest.mark.parametrize("maxlen,hd,ext", [(4096, 128, None), (64, 64, None), (300, 128, "longrope")])
 def test_rotary_tables_bit_exact_with_oracle(lib, maxlen, hd, ext):
     e = None
