@@ -67,6 +67,25 @@ int oumu_step_end(const void *stop_logits, const void *patch, void *patches, int
                   int min_len, int max_steps, oumu_stream_t stream);
 
 /*
+ * The decoding loop as one graph launch, with the stop test on the device: Engine::decode (src/model.rs:777-796)
+ * replays the step graph and reads `stop` back after every step; this runs
+ *     while (ctr[1] < max_steps && some stop[s] < 0 for s < B) { step; }
+ * as a CUDA WHILE conditional node around a copy of `step_graph` (a cudaGraph_t, e.g. torch's
+ * CUDAGraph(keep_graph=True).raw_cuda_graph(); it may hold kernel, memset, memcpy and child-graph nodes only),
+ * so the host reads `stop` once, after the loop. `stop` [B], `ctr` [4] (ctr[1] = patches so far, advanced by the
+ * step's oumu_step_end) and `status` [2] are device int buffers the step graph and the loop share; after a launch
+ * status[0] = steps run and status[1] = 1 if the loop ended at max_steps steps while ctr[1] had not reached
+ * max_steps (a step graph that does not advance ctr[1]), else 0. The loop holds its own copy of the step graph:
+ * `step_graph` may be destroyed after create. One loop per step graph may exist at a time (a CUDA rule for graphs
+ * with conditional nodes).
+ */
+typedef struct oumu_decode_loop_s *oumu_decode_loop_t;
+int oumu_decode_loop_create(void *step_graph, const int *stop, const int *ctr, int *status, int B, int max_steps,
+                            oumu_decode_loop_t *loop);
+int oumu_decode_loop_launch(oumu_decode_loop_t loop, oumu_stream_t stream);
+int oumu_decode_loop_destroy(oumu_decode_loop_t loop);
+
+/*
  * y[m][n] (row pitch ldy) = bf16(sum_k x[m][k] * W[n][k] (+ bias[n])) for m < M, n < N: x bf16 [M][K] with row
  * pitch ldx (>= K, a multiple of 8), W bf16 [N][K] contiguous, bias bf16 [N] or NULL, fp32 accumulation, one
  * rounding after the bias. K must be a multiple of 64; x and W 16-byte aligned. Replaces Lin::fwd -> Gpu::gemm

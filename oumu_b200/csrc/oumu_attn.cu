@@ -747,6 +747,83 @@ int oumu_step_end(const void *stop_logits, const void *patch, void *patches, int
     return OUMU_OK;
 }
 
+struct oumu_decode_loop_s {
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+};
+
+namespace {
+
+int add_loop_test(cudaGraphNode_t *node, cudaGraph_t g, const cudaGraphNode_t *dep, cudaGraphConditionalHandle h,
+                  const int *stop, const int *ctr, int *status, int B, int max_steps, int first) {
+    void *args[] = {&h, &stop, &ctr, &status, &B, &max_steps, &first};
+    cudaKernelNodeParams kp;
+    std::memset(&kp, 0, sizeof(kp));
+    kp.func = reinterpret_cast<void *>(glue::k_loop_test);
+    kp.gridDim = dim3(1);
+    kp.blockDim = dim3(256);
+    kp.kernelParams = args;
+    OUMU_CK(cudaGraphAddKernelNode(node, g, dep, dep ? 1 : 0, &kp));
+    return OUMU_OK;
+}
+
+int build_loop(oumu_decode_loop_s *L, cudaGraph_t step, const int *stop, const int *ctr, int *status, int B,
+               int max_steps) {
+    OUMU_CK(cudaGraphCreate(&L->graph, 0));
+    cudaGraphConditionalHandle h;
+    OUMU_CK(cudaGraphConditionalHandleCreate(&h, L->graph, 0, 0));
+    cudaGraphNode_t pre, loop, child, test;
+    int rc = add_loop_test(&pre, L->graph, nullptr, h, stop, ctr, status, B, max_steps, 1);
+    if (rc) return rc;
+    alignas(cudaGraphNodeParams) unsigned char raw[sizeof(cudaGraphNodeParams)] = {};  // zeroed: reserved fields
+    auto *cp = reinterpret_cast<cudaGraphNodeParams *>(raw);
+    cp->type = cudaGraphNodeTypeConditional;
+    cp->conditional.handle = h;
+    cp->conditional.type = cudaGraphCondTypeWhile;
+    cp->conditional.size = 1;
+    OUMU_CK(cudaGraphAddNode(&loop, L->graph, &pre, 1, cp));
+    cudaGraph_t body = cp->conditional.phGraph_out[0];
+    OUMU_CK(cudaGraphAddChildGraphNode(&child, body, nullptr, 0, step));
+    rc = add_loop_test(&test, body, &child, h, stop, ctr, status, B, max_steps, 0);
+    if (rc) return rc;
+    OUMU_CK(cudaGraphInstantiate(&L->exec, L->graph, 0));
+    return OUMU_OK;
+}
+
+}  // namespace
+
+int oumu_decode_loop_create(void *step_graph, const int *stop, const int *ctr, int *status, int B, int max_steps,
+                            oumu_decode_loop_t *loop) {
+    if (!loop) return OUMU_ERR_INVALID;
+    *loop = nullptr;
+    if (!step_graph || !stop || !ctr || !status || B < 1 || max_steps < 1) return OUMU_ERR_INVALID;
+    auto *L = new oumu_decode_loop_s;
+    const int rc = build_loop(L, static_cast<cudaGraph_t>(step_graph), stop, ctr, status, B, max_steps);
+    if (rc) {
+        oumu_decode_loop_destroy(L);
+        return rc;
+    }
+    *loop = L;
+    return OUMU_OK;
+}
+
+int oumu_decode_loop_launch(oumu_decode_loop_t loop, oumu_stream_t stream) {
+    if (!loop || !loop->exec) return OUMU_ERR_INVALID;
+    OUMU_CK(cudaGraphLaunch(loop->exec, reinterpret_cast<cudaStream_t>(stream)));
+    return OUMU_OK;
+}
+
+int oumu_decode_loop_destroy(oumu_decode_loop_t loop) {
+    if (!loop) return OUMU_OK;
+    cudaError_t e1 = cudaSuccess, e2 = cudaSuccess;
+    if (loop->exec) e1 = cudaGraphExecDestroy(loop->exec);
+    if (loop->graph) e2 = cudaGraphDestroy(loop->graph);
+    delete loop;
+    OUMU_CK(e1);
+    OUMU_CK(e2);
+    return OUMU_OK;
+}
+
 int oumu_gemm(const void *x, int ldx, const void *w, void *y, int ldy, const void *bias, int M, int N, int K,
               oumu_stream_t stream) {
     if (!gemm_args_ok(x, ldx, w, y, ldy, M, N, K)) return OUMU_ERR_INVALID;

@@ -196,4 +196,27 @@ __global__ void __launch_bounds__(256) k_step_end(const bf16 *stop_logits, const
     }
 }
 
+// Condition of the decoding loop (Engine::decode, src/model.rs:784-793): one more step while fewer than max_steps
+// patches exist (ctr[1]) and some take has not stopped (stop[s] < 0). One block; thread 0 sets the WHILE node's
+// condition. status[0] counts the steps the loop ran in this launch (the first test, upstream of the WHILE node,
+// resets it); the loop also ends after max_steps steps whatever ctr[1] says, with status[1] = 1, so a step that
+// failed to advance ctr[1] cannot keep the device in the loop.
+__global__ void __launch_bounds__(256) k_loop_test(cudaGraphConditionalHandle h, const int *stop, const int *ctr,
+                                                   int *status, int B, int max_steps, int first) {
+    int open = 0;
+    for (int s = threadIdx.x; s < B; s += blockDim.x) open |= stop[s] < 0;
+    open = __syncthreads_or(open);
+    if (threadIdx.x == 0) {
+        const int ran = first ? 0 : status[0] + 1;
+        bool more = open && ctr[1] < max_steps;
+        if (first) status[1] = 0;
+        if (more && ran >= max_steps) {
+            status[1] = 1;
+            more = false;
+        }
+        status[0] = ran;
+        cudaGraphSetConditional(h, more ? 1u : 0u);
+    }
+}
+
 }  // namespace glue

@@ -321,12 +321,13 @@ class Engine:
         ops.step_end(self.stop_l, self.x, self.patches, self.stop, self.ctr, self.lens, B, self.min_len,
                      self.max_steps)
 
-    def capture(self):
+    def capture(self, keep_graph=False):
         """The step as one CUDA graph (src/model.rs:779-783), programmatic edges into the decode layers. The step
-        runs once eagerly first (buffers, cuBLAS handles), which advances the state by one step."""
+        runs once eagerly first (buffers, cuBLAS handles), which advances the state by one step. keep_graph=True
+        keeps the cudaGraph_t for decode(device_loop=True) and instantiates the graph for replay."""
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream())
-        g = torch.cuda.CUDAGraph()
+        g = torch.cuda.CUDAGraph(keep_graph=keep_graph)
         with torch.cuda.stream(s):
             self.step()
             s.synchronize()
@@ -336,5 +337,33 @@ class Engine:
                     self.step()
             finally:
                 ops.set_pdl(prev)
+            if keep_graph:
+                g.instantiate()
         torch.cuda.current_stream().wait_stream(s)
         return g
+
+    def decode(self, graph, device_loop=True):
+        """Steps until every take has stopped or max_steps patches exist; the number of patches of every take
+        (Engine::decode, src/model.rs:777-796: stop step + 1, or max_steps for a take that never stopped).
+        device_loop=False replays `graph` and reads the stop flags after every step, as the reference does;
+        device_loop=True runs the whole loop as one graph launch with the stop test on the device (`graph` from
+        capture(keep_graph=True)) and reads the flags once."""
+        if device_loop:
+            if getattr(self, "_loop_graph", None) is not graph:
+                if getattr(self, "_loop", None) is not None:
+                    self._loop.close()
+                self.loop_status = torch.zeros(2, dtype=torch.int32, device=self.device)
+                self._loop = ops.DecodeLoop(graph, self.stop, self.ctr, self.loop_status, self.B, self.max_steps)
+                self._loop_graph = graph
+            self._loop.launch()
+            stops = self.stop.cpu()
+            if int(self.loop_status[1]) != 0:
+                raise RuntimeError("decoding loop ended at its step cap while ctr[1] < max_steps")
+        else:
+            stops = self.stop.cpu()
+            for _ in range(int(self.ctr[1]), self.max_steps):
+                if bool((stops >= 0).all()):
+                    break
+                graph.replay()
+                stops = self.stop.cpu()
+        return [int(v) + 1 if v >= 0 else self.max_steps for v in stops.tolist()]

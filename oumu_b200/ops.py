@@ -191,6 +191,40 @@ def step_end(stop_logits, patch, patches, stop, ctr, lens, B, min_len, max_steps
               max_steps, _stream())
 
 
+class DecodeLoop:
+    """The decoding loop of Engine::decode (src/model.rs:777-796) as one graph launch (oumu_decode_loop_*): the
+    step graph `step_graph` (a torch.cuda.CUDAGraph captured with keep_graph=True) repeated inside a CUDA WHILE node
+    while ctr[1] < max_steps and some stop[s] < 0, the test made on the device after every step. `status` (int32 [2],
+    device) receives the steps run and the iteration-cap flag of each launch."""
+
+    def __init__(self, step_graph, stop, ctr, status, B, max_steps):
+        import ctypes
+        for t in (stop, ctr, status):
+            if t.dtype != torch.int32 or not t.is_cuda or not t.is_contiguous():
+                raise ValueError("DecodeLoop: stop, ctr and status are contiguous int32 device tensors")
+        if stop.numel() < B or ctr.numel() < 2 or status.numel() < 2:
+            raise ValueError("DecodeLoop: stop [B], ctr [>= 2] and status [2]")
+        h = ctypes.c_void_p()
+        _lib.call("oumu_decode_loop_create", step_graph.raw_cuda_graph(), _p(stop), _p(ctr), _p(status), B,
+                  max_steps, ctypes.byref(h))
+        self._h = h
+        self._keep = (stop, ctr, status)  # the loop's kernels hold these pointers
+
+    def launch(self):
+        _lib.call("oumu_decode_loop_launch", self._h, _stream())
+
+    def close(self):
+        if self._h is not None and self._h.value:
+            _lib.call("oumu_decode_loop_destroy", self._h)
+        self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def gemm(x, w, y, bias=None):
     """y[M][N] = bf16(x[M][K] . w[N][K]^T (+ bias)) on the tensor cores; x and y may be row-strided views."""
     M, K = x.shape

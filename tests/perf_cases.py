@@ -12,6 +12,8 @@ CASE: decode (config 2: 64 takes, slots of 4096, lengths U[330,4096]; per layer)
       prefill_kv (config 3 per layer in one launch: prefill + k/v into all 64 slots; and the separate launches)
       locdit (config 4: 512 sequences x 12 tokens, 16 heads, hd 64)
       locdit_ref (the reference's DiT shape: 512 sequences x 11 tokens, 16 q / 2 kv heads, hd 128)
+      loop (config 5 decoding loop, 32 takes, --reps steps: host loop reading the stop flags after every replay
+            against the same graph inside one launch with the stop test on the device; per step)
 Prints one JSON line: mean milliseconds per launch (CUDA events on the launching stream, after warm-up) and the
 algorithmic bytes / FLOPs per launch. With --impl ref and per-take lengths, the reference kernel (one shared
 position) runs once per take with slot-offset pointers; "decode_shared" instead runs every take at the mean length.
@@ -140,6 +142,31 @@ def case_step(args, lens):
     return dict(ms=ms, bytes=nbytes, GBps=nbytes / ms / 1e6, pdl=args.pdl)
 
 
+def case_loop(args, B=32):
+    """Config 5: `reps` decoding steps of the captured step graph, (a) replayed from the host loop of
+    Engine::decode (src/model.rs:784-793: one replay, then the stop flags read back, per step) and (b) as one launch
+    of the device-side loop (ops.DecodeLoop). No take asks to stop early (min_len above max_steps), so both run the
+    same steps; milliseconds per step, wall clock around the whole loop (it includes the host reads)."""
+    import time
+    from oumu_b200 import engine
+    steps = args.reps
+    e = engine.Engine(B, max_steps=steps + 1, min_len=10 ** 6)
+    e.prime([int(v) for v in synth.uniform_int(synth.config_seed(5), B, 330, 4096 - 2 * steps - 8)])
+    g = e.capture(keep_graph=True)  # the capture's eager step is step 1
+    s0 = [t.clone() for t in (e.ctr, e.stop, e.lens)]
+    out = {}
+    for mode in ("host", "device", "host", "device"):  # the first pair warms up
+        for t, v in zip((e.ctr, e.stop, e.lens), s0):
+            t.copy_(v)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        e.decode(g, device_loop=mode == "device")
+        torch.cuda.synchronize()
+        out[mode] = (time.perf_counter() - t0) * 1e3 / steps
+        assert int(e.ctr[1]) == steps + 1
+    return dict(ms=out["device"], host_ms=out["host"], steps=steps, takes=B)
+
+
 def case_prefill(args, impl, T=1024):
     layers = args.layers
     qkv = [rnd((T, (NQ + 2 * NK) * HD), 300 + l) for l in range(layers)]
@@ -233,6 +260,8 @@ def main():
         r = case_replicate(args, args.impl)
     elif c == "prefill_kv":
         r = case_prefill_kv(args)
+    elif c == "loop":
+        r = case_loop(args)
     elif c == "locdit":
         r = case_small(args, args.impl, 512, 12, 16, 16, 64)
     elif c == "locdit_ref":

@@ -90,6 +90,17 @@ def test_invalid_arguments_of_the_fused_and_step_entry_points(lib):
     assert lib.oumu_step_end(P, P, P, P, P, P, 4, 2, 0, None) == _lib.ERR_INVALID
     # projection GEMM: K not a multiple of its 64-element tile
     assert lib.oumu_gemm(P, 100, P, P, 128, None, 4, 128, 100, None) == _lib.ERR_INVALID
+    # decoding loop: no step graph, no status buffer, no takes, no steps; the handle is cleared on failure;
+    # launching a null loop is rejected and destroying one is a no-op
+    h = ctypes.c_void_p(1234)
+    assert lib.oumu_decode_loop_create(None, P, P, P, 4, 8, ctypes.byref(h)) == _lib.ERR_INVALID
+    assert h.value is None
+    assert lib.oumu_decode_loop_create(P, P, P, None, 4, 8, ctypes.byref(h)) == _lib.ERR_INVALID
+    assert lib.oumu_decode_loop_create(P, P, P, P, 0, 8, ctypes.byref(h)) == _lib.ERR_INVALID
+    assert lib.oumu_decode_loop_create(P, P, P, P, 4, 0, ctypes.byref(h)) == _lib.ERR_INVALID
+    assert lib.oumu_decode_loop_create(P, P, P, P, 4, 8, None) == _lib.ERR_INVALID
+    assert lib.oumu_decode_loop_launch(None, None) == _lib.ERR_INVALID
+    assert lib.oumu_decode_loop_destroy(None) == _lib.OK
 
 
 @pytest.mark.parametrize("maxlen,hd,ext", [(4096, 128, None), (64, 64, None), (300, 128, "longrope")])
