@@ -507,6 +507,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     TileIt it;
     it.seek(ta, pre, Ls, B);
+    if (ta + warp < tb) {
+        // L2 prefetch of the q rows (and rotary-table rows) of this warp's first segment before the wait, so the q
+        // load after it finds them in L2. A hint only: q written by the preceding kernel is still read correctly.
+        TileIt f = it;
+        for (int k = 0; k < warp; k++) f.next(Ls, nk);
+        const char *q = reinterpret_cast<const char *>(P.qkv + static_cast<long>(f.s) * (P.nq + 2 * nk) * HD +
+                                                       f.kh * G * HD);
+        if (lane * 128 < G * HD * 2) prefetch_l2(q + lane * 128);
+        if (FUSED && P.cos_t && lane < 2 * (HD * 2 / 128)) {
+            const float *tab = lane < HD * 2 / 128 ? P.cos_t : P.sin_t;
+            prefetch_l2(tab + static_cast<long>(f.L - 1) * (HD / 2) + (lane % (HD * 2 / 128)) * 32);
+        }
+    }
     pdl_wait();           // q is written upstream
     int owner = 0;
     uint32_t ntile = 0;   // tiles this warp has taken: its k-th tile is in stage warp + (k & 1) * NCW
