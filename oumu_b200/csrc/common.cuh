@@ -31,6 +31,24 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
     return __bfloat1622float2(v);
 }
 
+// Named barrier ID over N threads that also ANDs `pred` over them: every participating thread gets the same result,
+// so a loop that leaves on it leaves uniformly (no thread is left waiting at the barrier's next use).
+template <int ID, int N>
+__device__ __forceinline__ bool bar_and(bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(pred)), "n"(ID), "n"(N)
+        : "memory");
+    return r != 0;
+}
+// max(a, b, c) in one instruction (the three-input max.f32 of sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
 __device__ __forceinline__ uint64_t globaltimer() {
     uint64_t t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

@@ -41,7 +41,8 @@ struct Cfg {
     static constexpr int V_OFF = K_OFF + 2 * NBOX * BOX;     // 2 stages
     static constexpr int BAR_OFF = V_OFF + 2 * NBOX * BOX;
     static constexpr int LX_OFF = BAR_OFF + 128;             // the two halves of the row sums, 2 x 128 floats
-    static constexpr int SMEM = LX_OFF + 1024 + 1024;        // + alignment slack
+    static constexpr int MX_OFF = LX_OFF + 1024;             // half-row maxima, [tile parity][warpgroup][128]
+    static constexpr int SMEM = MX_OFF + 2048 + 1024;        // + alignment slack
     // TMEM: S (128 columns), two P buffers (hi: 64 columns of bf16 pairs, lo: 64), O (hd columns)
     static constexpr uint32_t TMEM_COLS = 512;
     static constexpr uint32_t P_COL = 128, O_COL = 384;
@@ -238,44 +239,46 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         constexpr int OH = HD / 2;          // O columns per warpgroup
         float m = -INFINITY, l = 0.f;       // max in log2 units of the scaled score; this thread's half of the sum
         bool ok = true;
-        for (int j = 0; j < ntiles && ok; j++) {
-            ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL), j & 1));
-            if (!ok) break;
-            tc_fence_after();
+        // Every softmax thread reaches the per-tile barrier in every iteration and the loop is left only on its
+        // vote, so a wait that times out in one warp cannot leave the others at the barrier.
+        for (int j = 0; j < ntiles; j++) {
+            bool okt = ok && __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL), j & 1));
             // keys [0, kmax) are visible; only the causal diagonal tile and a ragged last tile need the mask
             const int kbase = j * BN;
             const bool masked = (causal && kbase + BN - 1 > q0) || kbase + BN > seq;
             const int kmax = (causal ? min(seq, qrow + 1) : seq) - kbase;
-            // the row max over all 128 columns (both warpgroups compute the same value)
-            float mt8[8];
-#pragma unroll
-            for (int k = 0; k < 8; k++) mt8[k] = -INFINITY;
-#pragma unroll
-            for (int c0 = 0; c0 < BN; c0 += 32) {
-                uint32_t sc[32];
-                tmem_ld32(tS + c0, sc);
-                tc_wait_ld();
-#pragma unroll
-                for (int c = 0; c < 32; c++) {
-                    const float v = (masked && c0 + c >= kmax) ? -INFINITY : __uint_as_float(sc[c]);
-                    mt8[c & 7] = fmaxf(mt8[c & 7], v);
-                }
-            }
-            const float mt = fmaxf(fmaxf(fmaxf(mt8[0], mt8[1]), fmaxf(mt8[2], mt8[3])),
-                                   fmaxf(fmaxf(mt8[4], mt8[5]), fmaxf(mt8[6], mt8[7]))) * sl2;
-            // this warpgroup's 64 columns
+            // this warpgroup's 64 columns of the row in one batch of loads; the row max meets its other half
+            // through shared memory at the barrier
             uint32_t sr[64];
-            tmem_ld32(tS + cb, sr);
-            tmem_ld32(tS + cb + 32, sr + 32);
-            tc_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(B_SFREE));
-            if (masked) {
+            float *mx = reinterpret_cast<float *>(sm + C::MX_OFF) + (j & 1) * 2 * BM;
+            float mh = -INFINITY;
+            if (okt) {
+                tc_fence_after();
+                tmem_ld32(tS + cb, sr);
+                tmem_ld32(tS + cb + 32, sr + 32);
+                tc_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(B_SFREE));
+                if (masked) {  // CTA-uniform: only the causal diagonal tile and a ragged last tile
 #pragma unroll
-                for (int c = 0; c < 64; c++)
-                    if (cb + c >= kmax) sr[c] = __float_as_uint(-INFINITY);
+                    for (int c = 0; c < 64; c++)
+                        if (cb + c >= kmax) sr[c] = __float_as_uint(-INFINITY);
+                }
+                float mt6[6];
+#pragma unroll
+                for (int k = 0; k < 6; k++) mt6[k] = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < 60; c += 2)
+                    mt6[(c >> 1) % 6] = fmax3(mt6[(c >> 1) % 6], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+                mh = fmax3(fmax3(mt6[0], mt6[1], mt6[2]), fmax3(mt6[3], mt6[4], mt6[5]),
+                           fmax3(__uint_as_float(sr[60]), __uint_as_float(sr[61]),
+                                 fmaxf(__uint_as_float(sr[62]), __uint_as_float(sr[63]))));
+                mx[wg * BM + r] = mh;
             }
+            ok = bar_and<2, 256>(okt);
+            if (!ok) break;
+            const float mt = fmaxf(mh, mx[(1 - wg) * BM + r]) * sl2;
             // lazy rescaling: keep the stale max unless the new one exceeds it by more than 2^RESCALE_LOG2
             float alpha = 1.f;
             if (mt > m + RESCALE_LOG2) {
@@ -294,16 +297,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
             l = l * alpha + rs;
-            // P_j goes into buffer j & 1 once PV_{j-2} has read it; O may be rescaled once PV_{j-1} has completed
-            if (j >= 2) {
-                ok = __all_sync(0xffffffffu, mbar_wait(bar(B_PDONE0 + (j & 1)), ((j >> 1) - 1) & 1));
-                if (!ok) break;
-            }
-            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+            // P_j goes into buffer j & 1 once PV_{j-2} has read it; O may be rescaled once PV_{j-1} has completed.
+            // A wait that times out here ends the loop at the next tile's vote.
+            if (j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_PDONE0 + (j & 1)), ((j >> 1) - 1) & 1));
+            if (ok && j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
                 ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE), (j - 1) & 1));
-                if (!ok) break;
-                tc_fence_after();
-                {
+                if (ok) {
+                    tc_fence_after();
 #pragma unroll
                     for (int c = 0; c < OH; c += 32) {
                         uint32_t orow[32];
@@ -316,6 +316,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     tc_wait_st();
                 }
             }
+            if (!ok) continue;
             // this half of P row r (keys cb .. cb + 63) -> TMEM buffer j & 1 as bf16 pairs: hi (the bf16 of p) in
             // columns [32wg, 32wg + 32), lo (the rest) in [64 + 32wg, ...); sr[k] takes the k-th hi pair in place
             uint32_t lw[32];
