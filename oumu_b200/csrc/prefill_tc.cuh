@@ -2,7 +2,9 @@
 // prefill over the prompt (src/model.rs:688,701 -> full(..., causal = true)).
 //
 // One CTA per (128-query tile, q head, sequence). Warp roles:
-//   warp 0      TMA producer: Q tile once, then K/V tiles of 128 positions into a 2-stage ring
+//   warp 0      TMA producer: Q tile once, then K and V tiles of 128 positions into two 2-stage rings: a K stage is
+//               free again once its S = Q.K^T has completed, a V stage once its P.V has, so the K of tile j+2
+//               loads while P_j.V still runs
 //   warp 1      TMEM allocator and the single MMA-issuing thread:
 //                 S  = Q . K_j^T      (M=128 queries, N=128 keys, K=hd; A and B K-major, 128-B swizzle)
 //                 O += P_j . V_j      (M=128, N=hd, K=128 keys; A = P from tensor memory, B = V MN-major)
@@ -40,7 +42,7 @@ struct Cfg {
     static constexpr int K_OFF = Q_OFF + NBOX * BOX;         // 2 stages
     static constexpr int V_OFF = K_OFF + 2 * NBOX * BOX;     // 2 stages
     static constexpr int BAR_OFF = V_OFF + 2 * NBOX * BOX;
-    static constexpr int LX_OFF = BAR_OFF + 128;             // the two halves of the row sums, 2 x 128 floats
+    static constexpr int LX_OFF = BAR_OFF + 256;             // the two halves of the row sums, 2 x 128 floats
     static constexpr int MX_OFF = LX_OFF + 1024;             // half-row maxima, [tile parity][warpgroup][128]
     static constexpr int SMEM = MX_OFF + 2048 + 1024;        // + alignment slack
     // TMEM: S (128 columns), two P buffers (hi: 64 columns of bf16 pairs, lo: 64), O (hd columns)
@@ -49,8 +51,9 @@ struct Cfg {
 };
 
 // barrier slots (8 bytes each) inside the barrier area
-enum { B_Q = 0, B_KVF0 = 1, B_KVF1 = 2, B_KVE0 = 3, B_KVE1 = 4, B_SFULL = 5, B_SFREE = 6, B_PFULL = 7, B_ODONE = 8,
-       B_COPY = 9, B_PDONE0 = 10, B_PDONE1 = 11, B_TMEM = 12, B_ABORT = 13 };
+enum { B_Q = 0, B_KF0 = 1, B_KF1 = 2, B_KE0 = 3, B_KE1 = 4, B_SFULL = 5, B_SFREE = 6, B_PFULL = 7, B_ODONE = 8,
+       B_COPY = 9, B_PDONE0 = 10, B_PDONE1 = 11, B_TMEM = 12, B_ABORT = 13, B_VF0 = 14, B_VF1 = 15, B_VE0 = 16,
+       B_VE1 = 17 };
 
 template <int HD>
 __global__ void __launch_bounds__(NTHREADS, 1)
@@ -77,10 +80,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(bar(B_Q), 1);
-        mbar_init(bar(B_KVF0), 1);
-        mbar_init(bar(B_KVF1), 1);
-        mbar_init(bar(B_KVE0), 1);
-        mbar_init(bar(B_KVE1), 1);
+        mbar_init(bar(B_KF0), 1);
+        mbar_init(bar(B_KF1), 1);
+        mbar_init(bar(B_KE0), 1);
+        mbar_init(bar(B_KE1), 1);
+        mbar_init(bar(B_VF0), 1);
+        mbar_init(bar(B_VF1), 1);
+        mbar_init(bar(B_VE0), 1);
+        mbar_init(bar(B_VE1), 1);
         mbar_init(bar(B_SFULL), 1);
         mbar_init(bar(B_SFREE), 8);
         mbar_init(bar(B_PFULL), 8);
@@ -115,16 +122,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int cj = ntiles_all - 1 - qt, g = h % G;
         const int per = slots > 0 ? (slots + G - 1) / G : 0, s0 = g * per, s1 = min(slots, s0 + per);
         const bool copy = slots > 0 && causal && s0 < s1;
-        auto load_kv = [&](int stg, int tj, uint32_t fb) {
+        // K (v = 0) or V (v = 1) of key tile tj into stage stg, completing its bytes on barrier fb. tx > 0: this call
+        // is the barrier's one arrival, expecting tx bytes; tx == 0: the bytes count against an earlier expectation.
+        auto load_half = [&](int v, int stg, int tj, uint32_t fb, uint32_t tx) {
             if (lane == 0) {
-                mbar_expect_tx(fb, 2 * C::NBOX * BOX);
+                if (tx > 0) mbar_expect_tx(fb, tx);
 #pragma unroll
-                for (int bx = 0; bx < C::NBOX; bx++) {
-                    tma_load_2d(sm_s + C::K_OFF + (stg * C::NBOX + bx) * BOX, &tqkv, fb, (nq + kh) * HD + bx * 64,
-                                row0 + tj * BN);
-                    tma_load_2d(sm_s + C::V_OFF + (stg * C::NBOX + bx) * BOX, &tqkv, fb,
-                                (nq + nk + kh) * HD + bx * 64, row0 + tj * BN);
-                }
+                for (int bx = 0; bx < C::NBOX; bx++)
+                    tma_load_2d(sm_s + (v ? C::V_OFF : C::K_OFF) + (stg * C::NBOX + bx) * BOX, &tqkv, fb,
+                                (nq + (v ? nk : 0) + kh) * HD + bx * 64, row0 + tj * BN);
             }
             __syncwarp();
         };
@@ -137,16 +143,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             bulk_commit();
         };
+        // tile cj's K and V have both landed in stage cj & 1
+        auto landed = [&](int t) {
+            return __all_sync(0xffffffffu, mbar_wait(bar(B_KF0 + (t & 1)), (t >> 1) & 1) &&
+                                               mbar_wait(bar(B_VF0 + (t & 1)), (t >> 1) & 1));
+        };
         bool ok = true, stored = false;
         for (int j = 0; j < ntiles; j++) {
             const int st = j & 1;
-            if (j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KVE0 + st), ((j >> 1) - 1) & 1));
+            if (j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KE0 + st), ((j >> 1) - 1) & 1));
             ok = __all_sync(0xffffffffu, ok && *abort_flag == 0);
             if (!ok) break;
             if (copy && stored && j == cj + 2) bulk_wait_read();  // the copy of tile cj has read this stage
-            load_kv(st, j, bar(B_KVF0 + st));
+            load_half(0, st, j, bar(B_KF0 + st), C::NBOX * BOX);
+            if (j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_VE0 + st), ((j >> 1) - 1) & 1));
+            if (!ok) break;
+            load_half(1, st, j, bar(B_VF0 + st), C::NBOX * BOX);
             if (copy && j == cj + 1) {  // tile cj, requested one step ago, goes out as soon as it has landed
-                ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KVF0 + (cj & 1)), (cj >> 1) & 1));
+                ok = landed(cj);
                 if (!ok) break;
                 store_tile(cj & 1);
                 stored = true;
@@ -155,7 +169,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (ok && copy && !stored) {
             if (cj < ntiles) {
                 // the CTA's last tile: still in its stage
-                ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KVF0 + (cj & 1)), (cj >> 1) & 1));
+                ok = landed(cj);
                 if (ok) {
                     store_tile(cj & 1);
                     stored = true;
@@ -163,9 +177,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             } else {
                 // a tile this CTA does not attend to: into stage 0 once its last use there (tile jl) is done
                 const int jl = (ntiles - 1) & ~1;
-                ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KVE0), (jl >> 1) & 1));
+                ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KE0), (jl >> 1) & 1) &&
+                                                 mbar_wait(bar(B_VE0), (jl >> 1) & 1));
                 if (ok) {
-                    load_kv(0, cj, bar(B_COPY));
+                    load_half(0, 0, cj, bar(B_COPY), 2 * C::NBOX * BOX);
+                    load_half(1, 0, cj, bar(B_COPY), 0);
                     ok = __all_sync(0xffffffffu, mbar_wait(bar(B_COPY), 0));
                     if (ok) {
                         store_tile(0);
@@ -194,9 +210,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     tc_mma_ss(tS, a, b, idS, ks > 0 ? 1u : 0u);
                 }
                 tc_commit(bar(B_SFULL));
+                tc_commit(bar(B_KE0 + st));
             };
             if (ok && ntiles > 0) {
-                ok = mbar_wait(bar(B_KVF0), 0);
+                ok = mbar_wait(bar(B_KF0), 0);
                 if (ok) {
                     tc_fence_after();
                     issue_S(0);
@@ -205,12 +222,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int j = 0; ok && j < ntiles; j++) {
                 if (j + 1 < ntiles) {
                     // S_{j+1} may overwrite S_j once the softmax warps have read it
-                    ok = mbar_wait(bar(B_KVF0 + ((j + 1) & 1)), ((j + 1) >> 1) & 1) && mbar_wait(bar(B_SFREE), j & 1);
+                    ok = mbar_wait(bar(B_KF0 + ((j + 1) & 1)), ((j + 1) >> 1) & 1) && mbar_wait(bar(B_SFREE), j & 1);
                     if (!ok) break;
                     tc_fence_after();
                     issue_S(j + 1);
                 }
-                ok = mbar_wait(bar(B_PFULL), j & 1);
+                ok = mbar_wait(bar(B_PFULL), j & 1) && mbar_wait(bar(B_VF0 + (j & 1)), (j >> 1) & 1);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t vbase = sm_s + C::V_OFF + (j & 1) * C::NBOX * BOX;
@@ -223,7 +240,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
                 tc_commit(bar(B_ODONE));
                 tc_commit(bar(B_PDONE0 + (j & 1)));
-                tc_commit(bar(B_KVE0 + (j & 1)));
+                tc_commit(bar(B_VE0 + (j & 1)));
             }
             if (!ok) *abort_flag = 1;
         }
