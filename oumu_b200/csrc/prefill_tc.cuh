@@ -148,22 +148,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             return __all_sync(0xffffffffu, mbar_wait(bar(B_KF0 + (t & 1)), (t >> 1) & 1) &&
                                                mbar_wait(bar(B_VF0 + (t & 1)), (t >> 1) & 1));
         };
+        // The V loads trail the K loads by one tile (K0, K1, V0, K2, V1, ...): K_j waits only for S_{j-2}, never
+        // behind the wait of a V stage for its P.V.
         bool ok = true, stored = false;
-        for (int j = 0; j < ntiles; j++) {
-            const int st = j & 1;
-            if (j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KE0 + st), ((j >> 1) - 1) & 1));
-            ok = __all_sync(0xffffffffu, ok && *abort_flag == 0);
-            if (!ok) break;
-            if (copy && stored && j == cj + 2) bulk_wait_read();  // the copy of tile cj has read this stage
-            load_half(0, st, j, bar(B_KF0 + st), C::NBOX * BOX);
-            if (j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_VE0 + st), ((j >> 1) - 1) & 1));
-            if (!ok) break;
-            load_half(1, st, j, bar(B_VF0 + st), C::NBOX * BOX);
-            if (copy && j == cj + 1) {  // tile cj, requested one step ago, goes out as soon as it has landed
-                ok = landed(cj);
+        for (int j = 0; j <= ntiles; j++) {
+            if (j < ntiles) {
+                const int st = j & 1;
+                if (j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KE0 + st), ((j >> 1) - 1) & 1));
+                ok = __all_sync(0xffffffffu, ok && *abort_flag == 0);
                 if (!ok) break;
-                store_tile(cj & 1);
-                stored = true;
+                if (copy && stored && j == cj + 2) bulk_wait_read();  // the copy of tile cj has read this stage
+                load_half(0, st, j, bar(B_KF0 + st), C::NBOX * BOX);
+            }
+            if (j >= 1) {
+                const int v = j - 1, sv = v & 1;
+                if (v >= 2) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_VE0 + sv), ((v >> 1) - 1) & 1));
+                if (!ok) break;
+                load_half(1, sv, v, bar(B_VF0 + sv), C::NBOX * BOX);
+                if (copy && v == cj) {  // tile cj goes out as soon as both its halves have landed
+                    ok = landed(cj);
+                    if (!ok) break;
+                    store_tile(cj & 1);
+                    stored = true;
+                }
             }
         }
         if (ok && copy && !stored) {
