@@ -111,6 +111,13 @@ __device__ __forceinline__ int atomic_add_acq_rel(int *p, int v) {
     return old;
 }
 
+// Load at GPU scope with acquire semantics: reads after it see the writes released by whoever produced the value.
+__device__ __forceinline__ int ld_acquire_gpu(const int *p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Non-blocking test of phase completion.
 __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;

@@ -193,33 +193,50 @@ __device__ __forceinline__ void merge_segment(const Params &P, const float *F, i
         store(Lsum);
         return;
     }
-    float *rec = P.part + (static_cast<long>(c) * 2 + slot) * C::PART_FLOATS;
-    if (lane == 0) {
+    const int cf = cta_of(Sg, W, Gc), cl = cta_of(Eg - 1, W, Gc);
+    // Every other contributor already published (the usual case at a CTA's end: the next CTA streamed its part of
+    // this segment first): this CTA is the last one, and merges without publishing its own partial.
+    if (tid == 0) *bcast = ld_acquire_gpu(P.cnt + g);
+    sync();
+    const bool own_in_regs = *bcast == cl - cf;
+    sync();
+    if (!own_in_regs) {
+        float *rec = P.part + (static_cast<long>(c) * 2 + slot) * C::PART_FLOATS;
+        if (lane == 0) {
+#pragma unroll
+            for (int k = 0; k < NH; k++) {
+                if (hb + k * HS >= GMAX) continue;
+                rec[hb + k * HS] = Mx[k];
+                rec[GMAX + hb + k * HS] = Lsum[k];
+            }
+        }
 #pragma unroll
         for (int k = 0; k < NH; k++) {
             if (hb + k * HS >= GMAX) continue;
-            rec[hb + k * HS] = Mx[k];
-            rec[GMAX + hb + k * HS] = Lsum[k];
+            float *ro = rec + 2 * GMAX + (hb + k * HS) * HD + d0;
+            if constexpr (DL == 4) *reinterpret_cast<float4 *>(ro) = make_float4(o[k][0], o[k][1], o[k][2], o[k][3]);
+            else *reinterpret_cast<float2 *>(ro) = make_float2(o[k][0], o[k][1]);
         }
+        // publish: the threads' writes are ordered before thread 0's release by the barrier; the acquire side of
+        // the same atomic orders the last contributor's reads of the other partials after their writers' releases
+        sync();
+        if (tid == 0) *bcast = atomic_add_acq_rel(P.cnt + g, 1);
+        sync();
+        const int old = *bcast;
+        sync();
+        if (old != cl - cf) return;
     }
+    // last contributor: merge every CTA's partial of this segment in one online pass, in CTA order (this CTA's own
+    // from registers or from its record: the same values and the same arithmetic either way; the records of four
+    // contributors are loaded together: one round trip to L2 per four)
+    float Mo[NH], Lo[NH], oo[NH][DL];
 #pragma unroll
     for (int k = 0; k < NH; k++) {
-        if (hb + k * HS >= GMAX) continue;
-        float *ro = rec + 2 * GMAX + (hb + k * HS) * HD + d0;
-        if constexpr (DL == 4) *reinterpret_cast<float4 *>(ro) = make_float4(o[k][0], o[k][1], o[k][2], o[k][3]);
-        else *reinterpret_cast<float2 *>(ro) = make_float2(o[k][0], o[k][1]);
+        Mo[k] = Mx[k];
+        Lo[k] = Lsum[k];
+#pragma unroll
+        for (int e = 0; e < DL; e++) oo[k][e] = o[k][e];
     }
-    // publish: the threads' writes are ordered before thread 0's release by the barrier; the acquire side of the
-    // same atomic orders the last contributor's reads of the other partials after their writers' releases
-    sync();
-    if (tid == 0) *bcast = atomic_add_acq_rel(P.cnt + g, 1);
-    sync();
-    const int old = *bcast;
-    sync();
-    const int cf = cta_of(Sg, W, Gc), cl = cta_of(Eg - 1, W, Gc);
-    if (old != cl - cf) return;
-    // last contributor: merge every CTA's partial of this segment in one online pass (the records of four
-    // contributors are loaded together: one round trip to L2 per four)
     float M2[NH], L2[NH];
 #pragma unroll
     for (int k = 0; k < NH; k++) {
@@ -233,8 +250,16 @@ __device__ __forceinline__ void merge_segment(const Params &P, const float *F, i
         const long ac = static_cast<long>(cc) * W / Gc;
         const float *rc = P.part + (static_cast<long>(cc) * 2 + ((cc == cf && ac < Sg) ? 1 : 0)) * C::PART_FLOATS;
         float mc[NH], lc[NH], oc[NH][DL];
+        const bool own = own_in_regs && cc == c;
 #pragma unroll
         for (int k = 0; k < NH; k++) {
+            if (own) {
+                mc[k] = Mo[k];
+                lc[k] = Lo[k];
+#pragma unroll
+                for (int e = 0; e < DL; e++) oc[k][e] = oo[k][e];
+                continue;
+            }
             const int h = hb + k * HS < GMAX ? hb + k * HS : 0;
             mc[k] = __ldcg(rc + h);
             lc[k] = __ldcg(rc + GMAX + h);
