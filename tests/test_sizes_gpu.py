@@ -75,6 +75,38 @@ def test_decode_config2_layers_back_to_back(cuda):
     assert int(ws[: B * NK * 4].view(torch.int32).abs().sum()) == 0
 
 
+def test_decode_bit_identical_whatever_the_merge_path(cuda):
+    # The last contributor of a segment split across CTAs merges from its own registers when the others have
+    # published first, else through its own record: which one happens depends on timing. Launches of one layer in a
+    # graph of programmatically dependent launches (the timing of a step) all give the bits of one eager launch.
+    B, maxlen, reps = 64, 4096, 4
+    lens = synth.uniform_int(synth.config_seed(1), B, 330, 4096)
+    qkv, kc, vc, ln = decode_case(B, lens, maxlen, seed=33)
+    want, ws = run_decode(qkv, kc, vc, ln, B, maxlen)
+    outs = [torch.zeros_like(want) for _ in range(reps)]
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    prev = ops.set_pdl(True)
+    try:
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for o in outs:
+                    ops.attn_decode(qkv, kc, vc, o, ws, None, ln, B, NQ, NK, HD, maxlen, HD ** -0.5)
+    finally:
+        ops.set_pdl(prev)
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(16):
+        for o in outs:
+            o.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        for o in outs:
+            assert torch.equal(o.view(torch.int16), want.view(torch.int16))
+    assert int(ws[: B * NK * 4].view(torch.int32).abs().sum()) == 0
+    del g
+
+
 @pytest.mark.parametrize("nq,nk,hd", [(16, 2, 128), (16, 2, 64), (8, 8, 128), (12, 4, 64), (7, 1, 128)])
 def test_decode_shapes_and_lengths(cuda, nq, nk, hd):
     maxlen = 640
