@@ -194,12 +194,17 @@ __device__ __forceinline__ void merge_segment(const Params &P, const float *F, i
         return;
     }
     const int cf = cta_of(Sg, W, Gc), cl = cta_of(Eg - 1, W, Gc);
-    // Every other contributor already published (the usual case at a CTA's end: the next CTA streamed its part of
-    // this segment first): this CTA is the last one, and merges without publishing its own partial.
-    if (tid == 0) *bcast = ld_acquire_gpu(P.cnt + g);
-    sync();
-    const bool own_in_regs = *bcast == cl - cf;
-    sync();
+    // At the CTA's last segment end (the consumer warps' merge): when every other contributor has already published
+    // (the usual case: the next CTA streamed its part of this segment first), this CTA is the last one and merges
+    // without publishing its own partial. The merge warp's partials are CTAs' first segments, whose other
+    // contributors finish later, so it publishes directly without the extra round trip.
+    bool own_in_regs = false;
+    if constexpr (NT != 32) {
+        if (tid == 0) *bcast = ld_acquire_gpu(P.cnt + g);
+        sync();
+        own_in_regs = *bcast == cl - cf;
+        sync();
+    }
     if (!own_in_regs) {
         float *rec = P.part + (static_cast<long>(c) * 2 + slot) * C::PART_FLOATS;
         if (lane == 0) {
