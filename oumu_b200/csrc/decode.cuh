@@ -123,7 +123,8 @@ __device__ __forceinline__ int cta_of(long t, long W, int G) {
 // runs as soon as they are read (the merger hands the flush buffer back to the consumers there, before its global
 // writes and the cross-CTA round trips). Writes the segment's output when the whole segment is in this CTA;
 // otherwise this CTA's partial, and if it is the last contributor (atomic counter) merges every contributor's
-// partial and writes the output.
+// partial and writes the output. At the CTA's last segment end, a CTA that finds every other contributor already
+// published is the last one and merges with its own partial still in registers, publishing nothing.
 template <int HD, int NT, class Release>
 __device__ __forceinline__ void merge_segment(const Params &P, const float *F, int s, int kh, long Sg, long Eg,
                                               long ta, long tb, long W, int Gc, int c, int slot, int tid,

@@ -4,20 +4,21 @@
 // One CTA per (128-query tile, q head, sequence). Warp roles:
 //   warp 0      TMA producer: Q tile once, then K and V tiles of 128 positions into two 2-stage rings: a K stage is
 //               free again once its S = Q.K^T has completed, a V stage once its P.V has, so the K of tile j+2
-//               loads while P_j.V still runs
+//               loads while P_j.V still runs (the V loads trail the K loads by one tile)
 //   warp 1      TMEM allocator and the single MMA-issuing thread:
 //                 S  = Q . K_j^T      (M=128 queries, N=128 keys, K=hd; A and B K-major, 128-B swizzle)
 //                 O += P_j . V_j      (M=128, N=hd, K=128 keys; A = P from tensor memory, B = V MN-major)
 //   warps 2..9  softmax, two warpgroups: warpgroup g owns columns [64g, 64g+64) of every row (thread = row of its
-//               TMEM lane quarter). Each thread reads its whole S row from TMEM for the row max (the two halves of a
-//               row compute the same value, so nothing is exchanged), exponentiates its own 64 columns, keeps its
-//               half of the row sum, writes its half of P_j into TMEM as two bf16 matrices hi + lo (so the weights
-//               keep ~16 mantissa bits; O += P_hi.V + P_lo.V), in one of two P buffers: P_{j+1} is written while
-//               P_j.V runs, and a buffer is reused once the P.V two tiles back has read it. It rescales its half of
-//               the O row in TMEM
-//               when the max has grown by more than 2^8 (lazy rescaling: until then the stale max is kept, which
-//               changes no result because O and the sum use the same one). The halves of the sum meet once, at the
-//               end, and each warpgroup writes bf16(O * (1 / sum)) for its 64 columns.
+//               TMEM lane quarter). Each thread loads its 64 columns of S from TMEM in one batch and takes their
+//               max; the two half-row maxima meet in shared memory at a per-tile barrier of the two warpgroups
+//               (which also votes on whether every wait succeeded, so the loop is left uniformly). It then
+//               exponentiates its 64 columns, keeps its half of the row sum and writes its half of P_j into TMEM
+//               as two bf16 matrices hi + lo (so the weights keep ~16 mantissa bits; O += P_hi.V + P_lo.V), in one
+//               of two P buffers: P_{j+1} is written while P_j.V runs, and a buffer is reused once the P.V two
+//               tiles back has read it. It rescales its half of the O row in TMEM when the max has grown by more
+//               than 2^8 (lazy rescaling: until then the stale max is kept, which changes no result because O and
+//               the sum use the same one). The halves of the sum meet once, at the end, and each warpgroup writes
+//               bf16(O * (1 / sum)) for its 64 columns.
 // KV epilogue (oumu_attn_prefill_kv, slots > 0): the prompt's k and v also go into every take's cache slot, with TMA
 // tensor stores from the 128-byte-swizzled tiles in shared memory through a map whose extent is the prompt length (rows
 // past it are never written). The CTA of query tile qt copies key tile ntiles - 1 - qt, the G q heads of a kv head
