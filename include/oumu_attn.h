@@ -116,8 +116,8 @@ int oumu_attn_decode(const void *qkv, const void *kc, const void *vc, void *out,
  * Decode attention that allocates nothing and takes no workspace: oumu_attn_decode with its scratch (split-KV
  * partials and combine counters) in a static device array of OUMU_DECODE_STATIC_SCRATCH_BYTES that the library
  * holds on every device that loads it, until the process exits. For callers that cannot give the library device
- * memory: a plug-in that sees only its input and output buffers, or a graph capture where allocating is not an
- * option. No counterpart in the reference (its att_part is allocated by the engine, src/model.rs:237).
+ * memory: a plug-in that receives only its input and output buffers from an engine that owns every device
+ * allocation, or a host whose memory policy forbids a library to allocate on its own. No counterpart in the reference (its att_part is allocated by the engine, src/model.rs:237).
  * The array holds one counter per (take, kv head) and at least one CTA's partials; shapes with more than about
  * 522,000 takes x kv heads do not fit and are rejected with OUMU_ERR_WORKSPACE and a message in
  * oumu_last_cuda_error (with fewer than one CTA per SM's worth of room the kernel runs on fewer CTAs). The first call on a device looks up the array's device

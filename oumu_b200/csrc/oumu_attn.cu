@@ -531,8 +531,8 @@ int oumu_attn_decode(const void *qkv, const void *kc, const void *vc, void *out,
 // Decode attention without a caller-supplied workspace.
 //
 // Some hosts cannot hand this library device memory for scratch: a plug-in that receives only its input and output
-// buffers from an engine that owns every device allocation, or a caller recording into a CUDA graph where a
-// cudaMalloc would break the capture and the per-call workspace was never planned for. For them the split-KV
+// buffers from an engine that owns every device allocation, or a host whose memory policy forbids a library to
+// allocate on its own (and whose workspace plan has no room for this kernel's scratch). For them the split-KV
 // partials and the combine counters live in this file-scope array instead: every device that loads the library
 // keeps its own copy, OUMU_DECODE_STATIC_SCRATCH_BYTES large, until the process exits.
 // ------------------------------------------------------------------------------------------------------------
