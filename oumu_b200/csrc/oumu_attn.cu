@@ -757,8 +757,7 @@ namespace {
 int add_loop_test(cudaGraphNode_t *node, cudaGraph_t g, const cudaGraphNode_t *dep, cudaGraphConditionalHandle h,
                   const int *stop, const int *ctr, int *status, int B, int max_steps, int first) {
     void *args[] = {&h, &stop, &ctr, &status, &B, &max_steps, &first};
-    cudaKernelNodeParams kp;
-    std::memset(&kp, 0, sizeof(kp));
+    cudaKernelNodeParams kp = {};  // shared memory 0, no extra launch options
     kp.func = reinterpret_cast<void *>(glue::k_loop_test);
     kp.gridDim = dim3(1);
     kp.blockDim = dim3(256);
