@@ -25,7 +25,7 @@ sys.path.insert(0, os.path.dirname(HERE))
 
 from oracle import refkern as rk  # noqa: E402
 from oumu_b200 import engine, synth  # noqa: E402
-from oumu_b200.engine import DIT_SEQ, DIT_X0, ENC_SEQ, EPS, FSQ, HD, LM, LOC, NK, NQ, PATCH  # noqa: E402
+from oumu_b200.engine import DIT_SEQ, DIT_X0, ENC_SEQ, EPS, FSQ, HD, LM, LOC, NK, NQ  # noqa: E402
 
 P, I, F = rk.P, rk.I, rk.F
 

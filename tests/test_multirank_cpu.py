@@ -4,7 +4,6 @@ import os
 import sys
 from datetime import timedelta
 
-import pytest
 import torch.multiprocessing as mp
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))

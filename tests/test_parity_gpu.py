@@ -1,6 +1,5 @@
 """Parity of the sm_100a library (through its C ABI) with the CPU oracle, with the golden outputs of the reference's
 own kernels, and with those kernels run live when their fatbin travelled with the tree."""
-import glob
 import json
 import os
 
