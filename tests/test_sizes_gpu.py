@@ -142,6 +142,31 @@ def test_decode_many_takes(cuda, B, maxlen, fused):
     gc.assert_close(u16(att), ref, f"{B} takes fused")
 
 
+@pytest.mark.parametrize("maxlen,hd,fused", [(100, 128, False), (100, 128, True), (72, 64, False)])
+def test_decode_slot_length_not_a_multiple_of_the_tile(cuda, maxlen, hd, fused):
+    # slots of a length that is not a multiple of the 32-position tile: a segment's last tile reaches into the next
+    # take's slot (masked) and, for the last take, past the end of the caches (the tensor map fills zeros)
+    lens = [1, 31, 32, 33, maxlen - 1, maxlen, 64, maxlen]
+    B = len(lens)
+    qkv, kc, vc, ln = decode_case(B, lens, maxlen, hd=hd, seed=50 + maxlen)
+    if not fused:
+        att, _ = run_decode(qkv, kc, vc, ln, B, maxlen, hd=hd)
+        gc.assert_close(u16(att), oracle_decode(qkv, kc, vc, lens, B, maxlen, hd=hd), f"maxlen {maxlen}")
+        return
+    qkv_h, kc_h, vc_h = u16(qkv), u16(kc), u16(vc)
+    att = torch.zeros((B, NQ * hd), dtype=torch.bfloat16, device="cuda")
+    ws = ops.decode_workspace(B, NQ, NK, hd, maxlen)
+    ops.step_tf_attention(qkv, kc, vc, att, ws, None, None, None, ln, B, NQ, NK, hd, maxlen, rope_on=False)
+    torch.cuda.synchronize()
+    for t, L in enumerate(lens):
+        kcs, vcs = np.ascontiguousarray(kc_h[t:t + 1]), np.ascontiguousarray(vc_h[t:t + 1])
+        cpu.kv_write(np.ascontiguousarray(qkv_h[t:t + 1]), kcs, vcs, L - 1, 1, 1, NQ, NK, hd, maxlen)
+        kc_h[t], vc_h[t] = kcs[0], vcs[0]
+    assert np.array_equal(u16(kc), kc_h) and np.array_equal(u16(vc), vc_h)
+    ref = cpu.attn_decode(qkv_h, kc_h, vc_h, None, np.asarray(lens, np.int32), B, NQ, NK, hd, maxlen, hd ** -0.5)
+    gc.assert_close(u16(att), ref, f"maxlen {maxlen} fused")
+
+
 def test_decode_rejects_takes_past_shared_memory(cuda):
     # the per-take tile prefix lives in shared memory: far more takes than the engine's 1024 are refused with
     # OUMU_ERR_UNSUPPORTED before any launch
