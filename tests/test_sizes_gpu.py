@@ -327,6 +327,20 @@ def test_prefill_vs_oracle(cuda, T, causal, hd, nq, nk):
     gc.assert_close(u16(out), ref, f"prefill T={T}")
 
 
+@pytest.mark.parametrize("causal", [1, 0])
+def test_prefill_several_sequences_vs_oracle(cuda, causal):
+    # three prompts of 200 tokens in one call: each sequence's ragged last tile reaches into the next one's rows,
+    # which the sequence bound masks
+    nseq, seq, nq, nk, hd = 3, 200, 16, 2, 128
+    rows, W = nseq * seq, (nq + 2 * nk) * hd
+    qkv = rand_bf16((rows, W), 95 + causal)
+    out = torch.zeros((rows, nq * hd), dtype=torch.bfloat16, device="cuda")
+    ops.attn_full(qkv, out, rows, seq, causal, nq, nk, hd, hd ** -0.5)
+    torch.cuda.synchronize()
+    ref = cpu.attn_full(u16(qkv), rows, seq, causal, nq, nk, hd, hd ** -0.5)
+    gc.assert_close(u16(out), ref, f"{nseq} x {seq} causal={causal}")
+
+
 @pytest.mark.parametrize("nseq,seq,nq,nk,hd", [(512, 12, 16, 16, 64), (512, 11, 16, 2, 128), (256, 5, 16, 2, 128)])
 def test_locdit_full_size_vs_oracle(cuda, nseq, seq, nq, nk, hd):
     # config 4 (256 takes x 2 CFG = 512 sequences of 12 tokens, 16 heads, hd 64) and the reference's DiT / LocEnc
