@@ -106,7 +106,8 @@ int oumu_attn_decode_reset(void *workspace, size_t workspace_bytes, int B, int n
  * the reference's sc.att [B][nq*hd], `workspace` takes the place of StepBufs::att_part (src/model.rs:237).
  * The workspace the reference allocates for att_part is always enough: with less than
  * oumu_attn_decode_workspace() bytes the kernel uses fewer CTAs, down to a minimum it checks.
- * Supported: hd in {64, 128}, nq / nk in 1..8.
+ * Supported: hd in {64, 128}, nq / nk in 1..8, B <= 4096 (B <= 1203 for hd 128: the per-take length table shares
+ * the kernel's shared memory with the KV stages), B * nk * maxlen < 2^31; other shapes OUMU_ERR_UNSUPPORTED.
  */
 int oumu_attn_decode(const void *qkv, const void *kc, const void *vc, void *out, void *workspace,
                      size_t workspace_bytes, const int *pos, const int *lens, int B, int nq, int nk, int hd,
@@ -117,13 +118,19 @@ int oumu_attn_decode(const void *qkv, const void *kc, const void *vc, void *out,
  * partials and combine counters) in a static device array of OUMU_DECODE_STATIC_SCRATCH_BYTES that the library
  * holds on every device that loads it, until the process exits. For callers that cannot give the library device
  * memory: a plug-in that receives only its input and output buffers from an engine that owns every device
- * allocation, or a host whose memory policy forbids a library to allocate on its own. No counterpart in the reference (its att_part is allocated by the engine, src/model.rs:237).
- * The array holds one counter per (take, kv head) and at least one CTA's partials; shapes with more than about
- * 522,000 takes x kv heads do not fit and are rejected with OUMU_ERR_WORKSPACE and a message in
- * oumu_last_cuda_error (with fewer than one CTA per SM's worth of room the kernel runs on fewer CTAs). The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress); make that first call before any stream capture. Every call clears the counters
- * (an asynchronous memset on `stream`) and then uses the shared array, so calls that can overlap on the GPU (other
- * streams, other host threads) race with each other: serialise them.
+ * allocation, or a host whose memory policy forbids a library to allocate on its own. No counterpart in the
+ * reference (its att_part is allocated by the engine, src/model.rs:237).
+ * Limits, checked before anything is queued (a rejected call leaves the stream and the array untouched):
+ *   - every limit of oumu_attn_decode: hd in {64, 128}, nq / nk in 1..8, B <= 4096, B * nk * maxlen < 2^31, and
+ *     the per-take length table in shared memory, which caps B at 1203 for hd 128 (OUMU_ERR_UNSUPPORTED);
+ *   - the array holds one counter per (take, kv head) plus at least one CTA's partials: B * nk <= 522,176 for
+ *     hd 128 and <= 523,200 for hd 64, else OUMU_ERR_WORKSPACE with a message in oumu_last_cuda_error. Below one
+ *     CTA per SM's worth of room the kernel runs on fewer CTAs.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress) with that device
+ * current, in its primary context, and keeps it: make that first call before any stream capture, and do not reset
+ * the device afterwards. Every call clears the counters (an asynchronous memset on `stream`) and then uses the
+ * shared array, so calls that can overlap on the GPU (other streams, other host threads) race with each other:
+ * serialise them.
  */
 #define OUMU_DECODE_STATIC_SCRATCH_BYTES (2 * 1024 * 1024)
 int oumu_attn_decode_static(const void *qkv, const void *kc, const void *vc, void *out, const int *pos,

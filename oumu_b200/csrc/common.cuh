@@ -155,6 +155,13 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// The two halves of a cluster barrier, for a thread that has work to do between them (each warp converged). A
+// CTA's shared memory may be accessed by its peers only after every CTA of the cluster has started: an arrive
+// right after set-up and a wait before the first remote access guarantee that.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 // Address of the same shared-memory location in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
     uint32_t r;

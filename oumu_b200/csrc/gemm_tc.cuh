@@ -104,6 +104,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // first half of a cluster barrier: the epilogue waits on it before its first store into a peer's inbox (a peer's
+    // shared memory may be written only once that peer has started); the wait overlaps the main loop
+    cluster_arrive_relaxed();
 
     if (warp == 0) {
         // ------------------------------ TMA producer ------------------------------
@@ -131,6 +134,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
         }
         __syncwarp();
+        cluster_wait();
     } else if (warp == 1) {
         // ------------------------------ MMA issuer ------------------------------
         if (lane == 0) {
@@ -152,6 +156,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (!ok) *abort_flag = 1;
         }
         __syncwarp();
+        cluster_wait();
     } else {
         // ------------------------------ accumulator -> the owners' inboxes ------------------------------
         const int quarter = warp & 3;
@@ -161,6 +166,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t dst = cluster_map(sm_s + C::INBOX_OFF + ((rank * rpo + (r - owner * rpo)) * TN) * 4,
                                          static_cast<uint32_t>(owner));
         const bool ok = __all_sync(0xffffffffu, mbar_wait(afull, 0));
+        cluster_wait();  // every CTA of the cluster has started: its inbox may be written
         if (ok) {
             tc_fence_after();
 #pragma unroll 1

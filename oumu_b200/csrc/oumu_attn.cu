@@ -491,21 +491,32 @@ int oumu_attn_decode_reset(void *workspace, size_t workspace_bytes, int B, int n
 }
 
 namespace {
-int decode_entry(bool fused, const void *qkv, const void *kc, const void *vc, void *out, void *workspace,
-                 size_t workspace_bytes, const float *cos_t, const float *sin_t, const int *pos, const int *lens, int B,
-                 int nq, int nk, int hd, int maxlen, float scale, oumu_stream_t stream) {
-    if (!qkv || !kc || !vc || !out || !workspace || (!pos && !lens)) return OUMU_ERR_INVALID;
+// Every argument check of the decode entry points except the workspace's, in one place: a call that fails any of
+// them has launched and queued nothing.
+int decode_check(const void *qkv, const void *kc, const void *vc, const void *out, const float *cos_t,
+                 const float *sin_t, const int *pos, const int *lens, int B, int nq, int nk, int hd, int maxlen,
+                 float scale) {
+    if (!qkv || !kc || !vc || !out || (!pos && !lens)) return OUMU_ERR_INVALID;
     if (B < 1 || nq < 1 || nk < 1 || nq % nk || maxlen < 1 || !(scale > 0.f)) return OUMU_ERR_INVALID;
     if ((cos_t == nullptr) != (sin_t == nullptr)) return OUMU_ERR_INVALID;
     if (!head_dim_ok(hd) || nq / nk > dec::GMAX || B > 4096) return OUMU_ERR_UNSUPPORTED;
     if (static_cast<long>(B) * nk * maxlen >= (1L << 31)) return OUMU_ERR_UNSUPPORTED;
-    if (!aligned16(qkv) || !aligned16(kc) || !aligned16(vc) || !aligned16(out) || !aligned16(workspace) ||
+    // the per-take length table and tile prefix live in shared memory beside the stages
+    const int lay = hd == 128 ? dec::Smem<128>{B}.bytes() : dec::Smem<64>{B}.bytes();
+    if (lay + 1024 > kSmemMax) return OUMU_ERR_UNSUPPORTED;
+    if (!aligned16(qkv) || !aligned16(kc) || !aligned16(vc) || !aligned16(out) ||
         (cos_t && (!aligned16(cos_t) || !aligned16(sin_t))))
         return OUMU_ERR_INVALID;
+    return OUMU_OK;
+}
+
+// Launch of a decode whose arguments passed decode_check.
+int decode_launch(bool fused, const void *qkv, const void *kc, const void *vc, void *out, void *workspace,
+                  size_t workspace_bytes, const float *cos_t, const float *sin_t, const int *pos, const int *lens,
+                  int B, int nq, int nk, int hd, int maxlen, float scale, cudaStream_t st) {
     int sms = 0;
     int rc = current_device(&sms);
     if (rc) return rc;
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (fused)
         return hd == 128 ? launch_decode<128, true>(qkv, kc, vc, out, workspace, workspace_bytes, pos, lens, cos_t,
                                                     sin_t, B, nq, nk, maxlen, scale, sms, st)
@@ -515,6 +526,16 @@ int decode_entry(bool fused, const void *qkv, const void *kc, const void *vc, vo
                                                  nullptr, B, nq, nk, maxlen, scale, sms, st)
                      : launch_decode<64, false>(qkv, kc, vc, out, workspace, workspace_bytes, pos, lens, nullptr,
                                                 nullptr, B, nq, nk, maxlen, scale, sms, st);
+}
+
+int decode_entry(bool fused, const void *qkv, const void *kc, const void *vc, void *out, void *workspace,
+                 size_t workspace_bytes, const float *cos_t, const float *sin_t, const int *pos, const int *lens, int B,
+                 int nq, int nk, int hd, int maxlen, float scale, oumu_stream_t stream) {
+    int rc = decode_check(qkv, kc, vc, out, cos_t, sin_t, pos, lens, B, nq, nk, hd, maxlen, scale);
+    if (rc) return rc;
+    if (!workspace || !aligned16(workspace)) return OUMU_ERR_INVALID;
+    return decode_launch(fused, qkv, kc, vc, out, workspace, workspace_bytes, cos_t, sin_t, pos, lens, B, nq, nk, hd,
+                         maxlen, scale, reinterpret_cast<cudaStream_t>(stream));
 }
 }  // namespace
 
@@ -543,7 +564,9 @@ void *g_static_scratch[kMaxDevices] = {};
 std::mutex g_static_mu;
 
 // Device address of the static scratch on the current device. In host code the array's name only stands for the
-// device symbol, so its address is looked up once per device (with that device current) and kept.
+// device symbol, so its device address is looked up once per device, with that device current, and kept. The kept
+// address belongs to the device's primary context as it was at that first call (the one torch and the runtime
+// use); a cudaDeviceReset afterwards would leave it stale.
 int static_scratch_ptr(void **out) {
     int d = 0;
     OUMU_CK(cudaGetDevice(&d));
@@ -564,22 +587,26 @@ extern "C" {
 int oumu_attn_decode_static(const void *qkv, const void *kc, const void *vc, void *out, const int *pos,
                             const int *lens, int B, int nq, int nk, int hd, int maxlen, float scale,
                             oumu_stream_t stream) {
-    if (B < 1 || nk < 1 || nq < 1 || nq % nk || !head_dim_ok(hd)) return OUMU_ERR_INVALID;
+    // every check of oumu_attn_decode first: a rejected call queues nothing on the stream and leaves the shared
+    // array as it was
+    int rc = decode_check(qkv, kc, vc, out, nullptr, nullptr, pos, lens, B, nq, nk, hd, maxlen, scale);
+    if (rc) return rc;
     // the scratch this shape needs: the combine counters, then one partial pair per CTA (at least one CTA)
-    const size_t cbytes = decode_counter_bytes(B, nk);
-    if (cbytes + decode_part_bytes(hd) > OUMU_DECODE_STATIC_SCRATCH_BYTES) {
+    const size_t cbytes = decode_counter_bytes(B, nk), need = cbytes + decode_part_bytes(hd);
+    if (need > OUMU_DECODE_STATIC_SCRATCH_BYTES) {
         std::snprintf(g_last_cuda, sizeof(g_last_cuda),
-                      "oumu_attn_decode_static: B * nk = %d needs %zu bytes of scratch, the static scratch holds %d",
-                      B * nk, cbytes + decode_part_bytes(hd), OUMU_DECODE_STATIC_SCRATCH_BYTES);
+                      "oumu_attn_decode_static: B * nk = %ld needs %zu bytes of scratch, the static scratch holds %d",
+                      static_cast<long>(B) * nk, need, OUMU_DECODE_STATIC_SCRATCH_BYTES);
         return OUMU_ERR_WORKSPACE;
     }
     void *ws = nullptr;
-    int rc = static_scratch_ptr(&ws);
+    rc = static_scratch_ptr(&ws);
     if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     // the counters must start at zero; the array keeps whatever the previous call (or an aborted one) left
-    OUMU_CK(cudaMemsetAsync(ws, 0, cbytes, reinterpret_cast<cudaStream_t>(stream)));
-    return decode_entry(false, qkv, kc, vc, out, ws, OUMU_DECODE_STATIC_SCRATCH_BYTES, nullptr, nullptr, pos, lens,
-                        B, nq, nk, hd, maxlen, scale, stream);
+    OUMU_CK(cudaMemsetAsync(ws, 0, cbytes, st));
+    return decode_launch(false, qkv, kc, vc, out, ws, OUMU_DECODE_STATIC_SCRATCH_BYTES, nullptr, nullptr, pos, lens,
+                         B, nq, nk, hd, maxlen, scale, st);
 }
 
 int oumu_attn_decode_step(void *qkv, void *kc, void *vc, void *out, void *workspace, size_t workspace_bytes,
