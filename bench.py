@@ -177,10 +177,20 @@ def cpu_inputs(lens, layers, seed):
     return out
 
 
+def host_threads():
+    """Host threads this process may run on. The oracle's OpenMP pool is set to it explicitly: torchrun exports
+    OMP_NUM_THREADS=1 to every rank, which would otherwise leave the CPU evaluation on one thread."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_time(lens, layers, min_seconds):
     """Times the oracle's decode attention over `layers` layers of the workload until min_seconds have passed;
     returns (GB/s, threads, seconds, sample description)."""
     from oracle import cpu
+    cpu.set_threads(host_threads())
     data = cpu_inputs(lens, layers, 7)
     ln = np.asarray(lens, np.int32)
     nbytes, reps, t0 = 0, 0, time.perf_counter()
@@ -199,6 +209,7 @@ def reference_arm(args, rank, world):
     if rank != 0:
         return 0
     from oracle import cpu
+    cpu.set_threads(host_threads())
     lens = take_lengths(0)
     data = cpu_inputs(lens, 1, 7)
     qkv, kc, vc = data[0]
@@ -223,10 +234,13 @@ def reference_arm(args, rank, world):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * dt / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1) bf16 q/k/v, per-take lengths U[330,4096])",
-        "config": {"workload": WORKLOAD, "takes_per_gpu": TAKES, "layers": LAYERS, "maxlen": MAXLEN},
+        "config": {"workload": WORKLOAD, "takes_per_gpu": TAKES, "layers": LAYERS, "maxlen": MAXLEN,
+                   "same_config": False,
+                   "sampled": f"a rate measured on a sample of the workload: each step is one layer of {group} of "
+                              f"the {TAKES} takes (rotating over them) on rank 0's host; GB/s of that sample"},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cpu.threads(), "kind": "port",
                          "sample": f"each step: one layer of {group} of the 64 takes (rotating), fp32 C "
-                                   "restatement of kernels/voxcpm.cu:131-185 (OpenMP)"},
+                                   "restatement of kernels/voxcpm.cu:131-185 (OpenMP, all host threads)"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference implements this path only as CUDA kernels; its CPU form is the oracle port",
     }
@@ -261,6 +275,8 @@ def patches_leg(args, dev, rank, max_over_ranks, sum_over_ranks, barrier, world=
     graph = e.capture()  # one eager step + the capture: each of this library's launches is called twice
     launches = (_lib.CALLS[0] - c0) // 2
 
+    local = []  # this rank's own times, for the per-rank record
+
     def timed(fn):
         e.set_lens(lens)
         for _ in range(W):
@@ -272,6 +288,7 @@ def patches_leg(args, dev, rank, max_over_ranks, sum_over_ranks, barrier, world=
             fn()
         b.record()
         torch.cuda.synchronize()
+        local.append(a.elapsed_time(b) / K)
         return max_over_ranks(a.elapsed_time(b))
 
     ms = timed(graph.replay)
@@ -313,6 +330,7 @@ def patches_leg(args, dev, rank, max_over_ranks, sum_over_ranks, barrier, world=
                 "path": "pinned host noise -> device, graph replay, patch + stop flags -> pinned host, host sync"},
         "gpu_launches_per_step": launches,
         "patches_gathered": gathered,
+        "_local_ms_per_step": local,
     }
 
 def main():
@@ -396,6 +414,15 @@ def main():
     def sum_over_ranks(x):
         return rank_reduce(x, "sum", dist if world > 1 else None, dev)
 
+    def per_rank(vals):
+        """Every rank's values (a list of floats of the same length on each rank), gathered to every rank."""
+        if world == 1:
+            return [list(vals)]
+        t = torch.tensor([float(v) for v in vals], dtype=torch.float64, device=dev)
+        out = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(out, t)
+        return [[float(x) for x in o.tolist()] for o in out]
+
     # ---- device-resident timing ----
     t_end = time.perf_counter() + 0.3
     while time.perf_counter() < t_end:  # let the clocks settle (untimed)
@@ -412,7 +439,8 @@ def main():
         e1.record()
         clocks.sample()  # the replays are queued: the GPU is busy with them now
         torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1))
+    ms_local = e0.elapsed_time(e1)
+    ms = max_over_ranks(ms_local)
     barrier()
     total_bytes = sum_over_ranks(per_step * args.steps)
     value = total_bytes / (ms / 1e3) / 1e9
@@ -433,7 +461,8 @@ def main():
             b.record()
             durs.append((a, b))
     torch.cuda.synchronize()
-    kern_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in durs))
+    kern_ms_local = statistics.mean(a.elapsed_time(b) for a, b in durs)
+    kern_ms = max_over_ranks(kern_ms_local)
     peak, peak_kind = measured_peak()
     traffic = committed_traffic()
 
@@ -490,13 +519,19 @@ def main():
     e2e_steps(args.steps)
     f1.record(s_comp)
     torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(f0.elapsed_time(f1))
+    e2e_ms_local = f0.elapsed_time(f1)
+    e2e_ms = max_over_ranks(e2e_ms_local)
     del graph2
     e2e_value = total_bytes / (e2e_ms / 1e3) / 1e9
     errword = ops.device_error()
     barrier()
 
     step = None if args.no_step else patches_leg(args, dev, rank, max_over_ranks, sum_over_ranks, barrier, world)
+    step_local = step.pop("_local_ms_per_step") if step else [0.0, 0.0]
+    # per-rank record (the line's times are the max over ranks): which GPU sets them, and at what clock
+    ck = clocks.summary()
+    ranks = per_rank([ms_local / args.steps, ms_local / (args.steps * LAYERS), kern_ms_local,
+                      e2e_ms_local / args.steps, ck["sm_mhz"] or 0.0, step_local[0], step_local[-1]])
 
     cpu_base = None
     if world == 1 and not args.no_cpu:
@@ -525,7 +560,11 @@ def main():
                     "path": "pinned host qkv -> device, graph of C-ABI calls, attention output -> pinned host; "
                             "double-buffered: the copies of neighbouring steps overlap a step's compute"},
             "cpu_baseline": cpu_base,
-            "clocks": clocks.summary(),
+            "clocks": ck,
+            "per_rank": [{"rank": r, "ms_per_step": round(v[0], 4), "kernel_ms": round(v[1], 5),
+                          "kernel_ms_alone": round(v[2], 5), "e2e_ms_per_step": round(v[3], 4),
+                          "sm_mhz_median": v[4], "patches_ms_per_step": round(v[5], 4),
+                          "patches_e2e_ms_per_step": round(v[6], 4)} for r, v in enumerate(ranks)],
             "gpu_launches": LAYERS * args.steps,
             "device_error": errword,
             "patches_per_s": step,

@@ -110,8 +110,23 @@ def attn_decode(qkv, kc, vc, part, att, pos, B, nq, nk, hd, maxlen, scale):
     launch("attn_combine", (B, nq, 1), hd, 0, [P(part), P(att), I(nq), I(hd), I(nsp)])
 
 
+_CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES = 8
+
+
+def _allow_smem(name, smem):
+    """Opt the kernel in to more than 48 KB of dynamic shared memory. The reference never does this
+    (src/gpu.rs:162-176 launches with the default limit), so its attn_full cannot launch for seq > 12160 at hd 128
+    ((hd + seq) * 4 bytes > 48 KB) although src/model.rs:411 accepts prompts of 16384 positions. The harness sets
+    the attribute so that the reference's arithmetic can still be compared at those lengths; the kernel is
+    unchanged."""
+    if smem > 48 * 1024:
+        _ck(_drv().cuFuncSetAttribute(_func(name), ctypes.c_int(_CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES),
+                                      ctypes.c_int(smem)), f"cuFuncSetAttribute {name}")
+
+
 def attn_full(qkv, out, rows, seq, causal, nq, nk, hd, scale):
     """src/model.rs:561-567: grid (rows, nq), block 128, dynamic smem (hd + seq) * 4."""
+    _allow_smem("attn_full", (hd + seq) * 4)
     launch("attn_full", (rows, nq, 1), 128, (hd + seq) * 4, [P(qkv), P(out), I(seq), I(int(bool(causal))), I(nq),
                                                              I(nk), I(hd), F(scale)])
 

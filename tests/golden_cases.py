@@ -233,13 +233,24 @@ ATOL = 2e-3   # north_star tolerance on bf16 outputs: max abs error 2e-3 ...
 RTOL = 1e-2   # ... and max relative error 1e-2 (element-wise |a - b| <= ATOL + RTOL * |b|)
 
 
+def _ordered(u):
+    """bf16 bit patterns (uint16) mapped to integers that count representable values in order (+0 and -0 both 0), so
+    that |ordered(a) - ordered(b)| is the distance of a and b in bf16 ulps."""
+    u = np.asarray(u).astype(np.int64)
+    mag = u & 0x7FFF
+    return np.where(u & 0x8000, -mag, mag)
+
+
 def compare(got, ref, atol=ATOL, rtol=RTOL):
     """Statistics of got vs ref (uint16 bf16 arrays): max abs error, max relative error over |ref| >= 1e-2,
-    count of elements outside |got - ref| <= atol + rtol * |ref|, exact-match fraction."""
+    count of elements outside |got - ref| <= atol + rtol * |ref|, exact-match fraction, and the elements whose
+    |got - ref| exceeds atol split into those exactly one bf16 ulp from ref and those further away."""
     g = synth.bf16_to_f32(got).astype(np.float64)
     r = synth.bf16_to_f32(ref).astype(np.float64)
     d = np.abs(g - r)
     big = np.abs(r) >= 1e-2
+    over = d > atol
+    ulps = np.abs(_ordered(got) - _ordered(ref))
     return dict(
         max_abs=float(d.max()) if d.size else 0.0,
         max_rel=float((d[big] / np.abs(r[big])).max()) if big.any() else 0.0,
@@ -247,11 +258,29 @@ def compare(got, ref, atol=ATOL, rtol=RTOL):
         exact=float((np.asarray(got) == np.asarray(ref)).mean()) if d.size else 1.0,
         n=int(d.size),
         nonfinite=int((~np.isfinite(g)).sum()),
+        over_atol=int(over.sum()),
+        over_atol_1ulp=int((over & (ulps == 1)).sum()),
+        over_atol_more=int((over & (ulps > 1)).sum()),
+        max_ulp_over_atol=int(ulps[over].max()) if over.any() else 0,
     )
+
+
+# Statistics of every tolerance comparison made in this process, by label (printed at the end of the pytest run by
+# tests/conftest.py, and written as JSON to $OUMU_PARITY_STATS when that is set).
+STATS = {}
+
+
+def _label(what):
+    import os
+    test = os.environ.get("PYTEST_CURRENT_TEST", "").split(" ")[0]
+    test = test[len("tests/"):] if test.startswith("tests/") else test
+    test = test.replace(".py::", "::")
+    return f"{test} {what}".strip()
 
 
 def assert_close(got, ref, what="", atol=ATOL, rtol=RTOL):
     st = compare(got, ref, atol, rtol)
+    STATS[_label(what)] = st
     assert st["nonfinite"] == 0 and st["bad"] == 0, f"{what}: {st}"
     return st
 
