@@ -196,6 +196,25 @@ int oumu_attn_prefill_kv(const void *qkv, void *out, void *kc, void *vc, int T, 
  */
 int oumu_device_error(int reset);
 
+/*
+ * Failure detection. No reference counterpart: the reference's kernels have no waits and report nothing
+ * (src/gpu.rs:11 only propagates launch errors).
+ *
+ * oumu_set_wait_limit_ns: the time after which a bounded device-side wait of this library's kernels (a pipeline
+ * stage that never fills, a hand-off that never comes) gives up: the kernel records OUMU_DEVERR_TIMEOUT in the
+ * device error word, stops waiting for anything, lets every copy it issued land and exits; its outputs are then
+ * unspecified, the decode workspace's counters are left at zero, and the context stays usable. Default 2 s; ns = 0
+ * restores it. Applies to the current device, to launches made after the call (a synchronous copy to the device:
+ * not inside a stream capture).
+ *
+ * oumu_test_drop_last_tile: fault injection for tests of that path, process-wide, off (0) by default; returns the
+ * previous setting. While on, every decode launch (oumu_attn_decode, oumu_attn_decode_static,
+ * oumu_attn_decode_step) leaves the last 32-position tile of its first CTA's range unloaded, so the consumer that
+ * owns it waits until the limit. Nothing faults, traps or hangs: the wait is bounded.
+ */
+int oumu_set_wait_limit_ns(unsigned long long ns);
+int oumu_test_drop_last_tile(int on);
+
 #ifdef __cplusplus
 }
 #endif

@@ -35,6 +35,8 @@ SIGNATURES = {
     "oumu_attn_prefill_kv": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _P]),
     "oumu_device_error": (_I, [_I]),
     "oumu_set_pdl": (_I, [_I]),
+    "oumu_set_wait_limit_ns": (_I, [ctypes.c_ulonglong]),
+    "oumu_test_drop_last_tile": (_I, [_I]),
     "oumu_rmsnorm": (_I, [_P, _P, _P, _P, _I, _I, _F, _P]),
     "oumu_silu_mul": (_I, [_P, _P, _I, _I, _P]),
     "oumu_pointwise": (_I, [_P, _L, _I, _F, _P]),

@@ -14,8 +14,10 @@ typedef __nv_bfloat16 bf16;
 // Defined here: the library is one translation unit (oumu_attn.cu includes every kernel header).
 __device__ unsigned int oumu_dev_error = 0;
 
-// A wait that has not finished after this many nanoseconds gives up and records OUMU_DEVERR_TIMEOUT.
-#define OUMU_WAIT_LIMIT_NS 2000000000ull
+// A wait that has not finished after this many nanoseconds gives up and records OUMU_DEVERR_TIMEOUT (2 s unless
+// oumu_set_wait_limit_ns changed it on this device).
+#define OUMU_WAIT_LIMIT_DEFAULT_NS 2000000000ull
+__device__ unsigned long long oumu_wait_limit_ns = OUMU_WAIT_LIMIT_DEFAULT_NS;
 
 __device__ __forceinline__ void record_error(unsigned int code) { atomicOr(&oumu_dev_error, code); }
 
@@ -129,13 +131,14 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 // Wait for the phase with the given parity to complete. Returns false (and records the error) when the wait
-// runs past OUMU_WAIT_LIMIT_NS; the caller then leaves its main loop.
+// runs past the device's wait limit (oumu_wait_limit_ns); the caller then leaves its main loop.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
-    uint64_t t0 = globaltimer();
+    const uint64_t t0 = globaltimer();
+    const uint64_t limit = *reinterpret_cast<volatile unsigned long long *>(&oumu_wait_limit_ns);
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 15u) == 0 && globaltimer() - t0 > OUMU_WAIT_LIMIT_NS) {
+        if ((it & 15u) == 0 && globaltimer() - t0 > limit) {
             record_error(OUMU_DEVERR_TIMEOUT);
             return false;
         }

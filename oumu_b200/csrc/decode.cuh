@@ -111,6 +111,9 @@ struct TileIt {
 };
 
 __device__ __forceinline__ void bar_consumers() { asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory"); }
+// End of the CTA's streaming: the consumer warps arrive (without waiting), the producer warp waits for them.
+__device__ __forceinline__ void bar_end_arrive() { asm volatile("bar.arrive 2, %0;" ::"n"((NCW + 1) * 32) : "memory"); }
+__device__ __forceinline__ void bar_end_sync() { asm volatile("bar.sync 2, %0;" ::"n"((NCW + 1) * 32) : "memory"); }
 
 // CTA whose tile range contains tile t (ranges [c*W/G, (c+1)*W/G)).
 __device__ __forceinline__ int cta_of(long t, long W, int G) {
@@ -381,7 +384,10 @@ __device__ __forceinline__ void rope_q_frags(uint32_t (&qb)[HD / 16][2], const f
     }
 }
 
-template <int HD, bool FUSED>
+// DROP: the fault-injection build used by the failure-detection tests (oumu_test_drop_last_tile): CTA 0 never loads
+// the last tile of its range, so the consumer that owns it waits until the limit; the producer then lets every copy
+// it issued land before the CTA exits. Everything else is the same code.
+template <int HD, bool FUSED, bool DROP = false>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_attn_decode(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, Params P) {
     using C = Cfg<HD>;
@@ -459,16 +465,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     if (warp == PRODUCER) {
         // ------------------------------ producer ------------------------------
+        int st = 0;
+        uint32_t use = 0;
         if (lane == 0) {
             tma_prefetch_desc(&tk);
             tma_prefetch_desc(&tv);
             TileIt it;
             it.seek(ta, pre, Ls, B);
-            int st = 0;
-            uint32_t use = 0;
+            const long tend = DROP && c == 0 ? tb - 1 : tb;
             // the unfused form reads the newest position only after the kernel that wrote it (the prologue)
             bool waited = FUSED;
-            for (long t = ta; t < tb; t++) {
+            for (long t = ta; t < tend; t++) {
                 if (!waited && it.j == it.T - 1) {
                     pdl_wait();
                     waited = true;
@@ -494,6 +501,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
             }
         }
+        // DROP build: once every consumer warp is done (a hardware barrier: the warp sleeps, no polling), after an
+        // abort (the consumers no longer wait for their tiles) this thread waits, bounded, until every load it
+        // issued has landed, since a copy must not write shared memory of a CTA that has left. Stage s's last load
+        // is of phase `use` if s < st, else of `use - 1` (none if use == 0). In the normal build the consumers have
+        // waited for every load.
+        if constexpr (DROP) {
+            __syncwarp();
+            bar_end_sync();
+            if (lane == 0 && misc[0]) {
+                for (int s2 = 0; s2 < STAGES; s2++) {
+                    if (s2 >= st && use == 0) continue;
+                    const uint32_t ph = s2 < st ? use : use - 1;
+                    mbar_wait(bar_full + 8 * s2, ph & 1u);
+                }
+            }
+        }
         return;
     }
 
@@ -506,12 +529,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (long t = ta; t < tb - 1; t++) {
             if (it.j == it.T - 1) {
                 const int b = nflush % NFB;
+                // after an abort (a wait that ran out anywhere in the CTA) nothing is waited for any more, but every
+                // merge still runs, on whatever the buffers hold: each contributor of a split segment still counts
+                // itself, so the segment's last contributor resets the counter and the workspace stays usable
                 const bool ok = __all_sync(0xffffffffu, misc[0] == 0 &&
                                                             mbar_wait(bar_ffull + 8 * b, (nflush / NFB) & 1));
-                if (!ok) {
-                    misc[0] = 1;
-                    break;
-                }
+                if (!ok) misc[0] = 1;
                 const long Sg = pre[it.s] + static_cast<long>(it.kh) * it.T;
                 merge_segment<HD, 32>(P, flush + b * NCW * C::PART_FLOATS, it.s, it.kh, Sg, Sg + it.T, ta, tb, W,
                                       Gc, c, nflush == 0 ? 0 : 1, lane, misc + 2, [&] {
@@ -717,6 +740,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         if (t + 1 < tb) it.next(Ls, nk);
         if (++owner == NCW) owner = 0;
+    }
+    if constexpr (DROP) {
+        __syncwarp();
+        bar_end_arrive();
     }
 }
 

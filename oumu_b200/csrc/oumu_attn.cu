@@ -36,6 +36,7 @@ int cuda_fail(cudaError_t e) {
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 std::atomic<int> g_pdl{0};
+std::atomic<int> g_drop_tile{0};  // oumu_test_drop_last_tile (off)
 
 // Launch with programmatic stream serialization when oumu_set_pdl(1) is in effect.
 template <typename... KArgs, typename... Args>
@@ -84,6 +85,14 @@ int current_device(int *sms) {
         OUMU_CK(cudaFuncSetAttribute(dec::k_attn_decode<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kSmemMax));
         OUMU_CK(cudaFuncSetAttribute(dec::k_attn_decode<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(dec::k_attn_decode<128, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(dec::k_attn_decode<64, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(dec::k_attn_decode<128, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(dec::k_attn_decode<64, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kSmemMax));
         OUMU_CK(cudaFuncSetAttribute(pf::k_attn_prefill<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      pf::Cfg<128>::SMEM));
@@ -230,8 +239,10 @@ int launch_decode(const void *qkv, const void *kc, const void *vc, void *out, vo
     P.nk = nk;
     P.maxlen = maxlen;
     P.sl2 = scale * 1.4426950408889634f;
-    OUMU_CK(launch_k(dec::k_attn_decode<HD, FUSED>, dim3(static_cast<unsigned>(grid)), dim3(dec::NTHREADS), smem, st,
-                     tk, tv, P));
+    // the fault-injection build only while oumu_test_drop_last_tile is on
+    OUMU_CK(launch_k(g_drop_tile.load(std::memory_order_relaxed) ? dec::k_attn_decode<HD, FUSED, true>
+                                                                  : dec::k_attn_decode<HD, FUSED, false>,
+                     dim3(static_cast<unsigned>(grid)), dim3(dec::NTHREADS), smem, st, tk, tv, P));
     return OUMU_OK;
 }
 
@@ -680,6 +691,14 @@ int oumu_kv_replicate(void *cache, int B, int nk, int maxlen, int hd, int T, oum
     OUMU_CK(cudaGetLastError());
     return OUMU_OK;
 }
+
+int oumu_set_wait_limit_ns(unsigned long long ns) {
+    const unsigned long long v = ns ? ns : OUMU_WAIT_LIMIT_DEFAULT_NS;
+    OUMU_CK(cudaMemcpyToSymbol(oumu_wait_limit_ns, &v, sizeof(v)));
+    return OUMU_OK;
+}
+
+int oumu_test_drop_last_tile(int on) { return g_drop_tile.exchange(on ? 1 : 0); }
 
 int oumu_device_error(int reset) {
     unsigned int v = 0;
