@@ -46,6 +46,7 @@ class RefStep(engine.Engine):
         super().__init__(B, lm_tc=(), **kw)
         self.part = torch.empty(B * NQ * (self.maxlen // 64) * (HD + 2), dtype=torch.float32, device=self.device)
         self.seeds = torch.arange(B, dtype=torch.int32, device=self.device)
+        self.noise_table = None  # [N][64][4] fp32: the noise kernel replays it (verification mode) instead of hashing
         self.z2 = {}
 
     def lin(self, lin, x, out):
@@ -109,7 +110,8 @@ class RefStep(engine.Engine):
         self.lin(self.lm_to_dit, self.lm_h, self.mu[:, :LOC])
         self.lin(self.res_to_dit, self.res_h, self.mu[:, LOC:])
         self.lin(self.dit_cond, self.cond.view(B * 4, 64), self.condp)
-        rk.launch("noise", (B, 1, 1), 256, 0, [P(self.x), P(None), P(self.ctr.data_ptr() + 4), P(self.seeds), I(B)])
+        rk.launch("noise", (B, 1, 1), 256, 0, [P(self.x), P(self.noise_table), P(self.ctr.data_ptr() + 4),
+                                               P(self.seeds), I(B)])
         for i, (_, dt) in enumerate(self.sched):
             self.lin(self.dit_in, self.x.view(B * 4, 64), self.xp)
             rk.launch("dit_build", (2 * B, DIT_SEQ, 1), 256, 0, [P(self.dit_seq), P(self.mu), P(self.temb[i]),
