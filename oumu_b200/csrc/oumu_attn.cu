@@ -4,6 +4,7 @@
 #include "../../include/oumu_attn.h"
 #include "../../include/oumu_step.h"
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdio>
@@ -17,6 +18,7 @@
 #include "full_small.cuh"
 #include "gemm_tc.cuh"
 #include "prefill_tc.cuh"
+#include "small_tc.cuh"
 #include "step_glue.cuh"
 
 namespace {
@@ -106,6 +108,18 @@ int current_device(int *sms) {
                                      fs::GCfg<64>::smem_bytes(fs::MAXM / fs::ROWS)));
         OUMU_CK(cudaFuncSetAttribute(fs::k_attn_small_grp<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      fs::GCfg<64>::smem_bytes(fs::MAXM / fs::ROWS)));
+        OUMU_CK(cudaFuncSetAttribute(sq::k_attn_small_tc<128, 16, 3, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(sq::k_attn_small_tc<128, 16, 3, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(sq::k_attn_small_tc<64, 16, 3, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(sq::k_attn_small_tc<64, 16, 3, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(sq::k_attn_small_tc<128, 128, 2, false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(sq::k_attn_small_tc<64, 128, 2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
         OUMU_CK(cudaFuncSetAttribute(gm::k_gemm<32, kGemmStages32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kSmemMax));
         OUMU_CK(cudaFuncSetAttribute(gm::k_gemm<64, kGemmStages64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -175,6 +189,30 @@ int make_map_cache(CUtensorMap *m, const void *base, int hd, int T, int planes, 
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         std::snprintf(g_last_cuda, sizeof(g_last_cuda), "cuTensorMapEncodeTiled (cache) failed (%d)",
+                      static_cast<int>(r));
+        return OUMU_ERR_CUDA;
+    }
+    return OUMU_OK;
+}
+
+// 3-D bf16 map over a [rows][heads][hd] buffer with row pitch row_bytes, box {64, bh, br}, 128-byte swizzle: a box
+// is br rows x bh heads x 64 columns, landing as bh * br rows of 128 bytes (row r, head h -> r * bh + h).
+int make_map_heads(CUtensorMap *m, const void *base, int hd, int heads, int rows, uint64_t row_bytes, uint32_t bh,
+                   uint32_t br) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) {
+        std::snprintf(g_last_cuda, sizeof(g_last_cuda), "cuTensorMapEncodeTiled unavailable");
+        return OUMU_ERR_CUDA;
+    }
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(hd), static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(hd) * 2, row_bytes};
+    cuuint32_t box[3] = {64, bh, br};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        std::snprintf(g_last_cuda, sizeof(g_last_cuda), "cuTensorMapEncodeTiled (heads) failed (%d)",
                       static_cast<int>(r));
         return OUMU_ERR_CUDA;
     }
@@ -270,6 +308,79 @@ int launch_small(const void *qkv, void *out, int rows, int seq, int causal, int 
     fs::k_attn_small<HD><<<static_cast<int>(grid), fs::WARPS * 32, smem, st>>>(
         static_cast<const bf16 *>(qkv), static_cast<bf16 *>(out), rows / seq, seq, causal, nq, nk,
         scale * 1.4426950408889634f);
+    OUMU_CK(cudaGetLastError());
+    return OUMU_OK;
+}
+
+// q heads per unit of the tensor-core short-sequence kernel: the largest divisor of the group (grouped heads) or of
+// nq (one q head per kv head, at most 8 stacked) with at most 128 stacked query rows.
+int small_tc_heads(int seq, int nq, int nk) {
+    const int G = nq / nk, top = G > 1 ? G : (nq < 8 ? nq : 8), of = G > 1 ? G : nq;
+    for (int d = top; d >= 1; d--)
+        if (of % d == 0 && d * seq <= 128) return d;
+    return 1;
+}
+
+// The persistent tensor-core kernel streams its units through a pipeline that takes ~5 us to fill and drain; with
+// fewer than 4 units per SM (the local encoder's 5-token calls, small batches) the one-CTA-per-unit kernel finishes
+// first, and for one q head per kv head (no group to stack) it is faster at every size measured.
+bool small_use_tc(int rows, int seq, int nq, int nk, int sms) {
+    const int G = nq / nk;
+    if (G < 2) return false;
+    const long units = static_cast<long>(rows / seq) * nk * (G / small_tc_heads(seq, nq, nk));
+    return units >= 4L * sms;
+}
+
+// Short sequences (seq <= 16) on the tensor cores (sq::k_attn_small_tc): the unit shape, the slots, the maps.
+template <int HD>
+int launch_small_tc(const void *qkv, void *out, int rows, int seq, int causal, int nq, int nk, float scale, int sms,
+                    cudaStream_t st, const float *cos_t = nullptr, const float *sin_t = nullptr) {
+    const int G = nq / nk;
+    const int HS = small_tc_heads(seq, nq, nk);
+    const int KS = G > 1 ? 1 : HS;
+    if (cos_t && KS != 1) return OUMU_ERR_UNSUPPORTED;  // rope fused only with grouped heads
+    sq::Params P;
+    P.cos_t = cos_t;
+    P.sin_t = sin_t;
+    P.seq = seq;
+    P.causal = causal ? 1 : 0;
+    P.nq = nq;
+    P.nk = nk;
+    P.G = G;
+    P.HS = HS;
+    P.KS = KS;
+    P.qrows = HS * seq;
+    P.krows = KS * seq;
+    P.ns = (P.krows + 15) / 16 * 16;
+    P.ups = G > 1 ? nk * (G / HS) : nq / HS;
+    const long units = static_cast<long>(rows / seq) * P.ups;
+    if (units > 0x7fffffffL) return OUMU_ERR_UNSUPPORTED;
+    P.units = static_cast<int>(units);
+    constexpr int NBOX = HD / 64;
+    P.qbox = (P.qrows * 128 + 1023) / 1024 * 1024;
+    P.kbox = P.ns * 128;
+    P.slot = NBOX * (P.qbox + 2 * P.kbox);
+    const int room = kSmemMax - sq::smem_bytes(0, 0);
+    P.nslot = room / P.slot < sq::NSLOT_MAX ? room / P.slot : sq::NSLOT_MAX;
+    if (P.nslot < 2) return OUMU_ERR_UNSUPPORTED;
+    P.sl2 = scale * 1.4426950408889634f;
+    const uint64_t wq = static_cast<uint64_t>(nq + 2 * nk) * HD * 2;
+    CUtensorMap tq, tkv, tout;
+    int rc = make_map_heads(&tq, qkv, HD, nq + 2 * nk, rows, wq, HS, seq);
+    if (rc) return rc;
+    rc = make_map_heads(&tkv, qkv, HD, nq + 2 * nk, rows, wq, KS, seq);
+    if (rc) return rc;
+    rc = make_map_heads(&tout, out, HD, nq, rows, static_cast<uint64_t>(nq) * HD * 2, HS, seq);
+    if (rc) return rc;
+    const int grid = P.units < sms ? P.units : sms;
+    // more than half an SM's shared memory, so that no two CTAs (each allocating all 512 TMEM columns) share an SM
+    const int smem = std::max(sq::smem_bytes(P.slot, P.nslot), 120 * 1024);
+    if (KS == 1) {
+        auto kern = cos_t ? sq::k_attn_small_tc<HD, 16, 3, true> : sq::k_attn_small_tc<HD, 16, 3, false>;
+        kern<<<grid, sq::nthreads(3), smem, st>>>(tq, tkv, tout, P);
+    } else {
+        sq::k_attn_small_tc<HD, 128, 2, false><<<grid, sq::nthreads(2), smem, st>>>(tq, tkv, tout, P);
+    }
     OUMU_CK(cudaGetLastError());
     return OUMU_OK;
 }
@@ -639,6 +750,9 @@ int oumu_attn_full(const void *qkv, void *out, int rows, int seq, int causal, in
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (seq <= fs::ROWS) {
+        if (small_use_tc(rows, seq, nq, nk, sms))
+            return hd == 128 ? launch_small_tc<128>(qkv, out, rows, seq, causal, nq, nk, scale, sms, st)
+                             : launch_small_tc<64>(qkv, out, rows, seq, causal, nq, nk, scale, sms, st);
         return hd == 128 ? launch_small<128>(qkv, out, rows, seq, causal, nq, nk, scale, sms, st)
                          : launch_small<64>(qkv, out, rows, seq, causal, nq, nk, scale, sms, st);
     }
@@ -659,6 +773,9 @@ int oumu_attn_full_rope(const void *qkv, void *out, const float *cos_t, const fl
     int rc = current_device(&sms);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (small_use_tc(rows, seq, nq, nk, sms))
+        return hd == 128 ? launch_small_tc<128>(qkv, out, rows, seq, causal, nq, nk, scale, sms, st, cos_t, sin_t)
+                         : launch_small_tc<64>(qkv, out, rows, seq, causal, nq, nk, scale, sms, st, cos_t, sin_t);
     return hd == 128 ? launch_small<128>(qkv, out, rows, seq, causal, nq, nk, scale, sms, st, cos_t, sin_t)
                      : launch_small<64>(qkv, out, rows, seq, causal, nq, nk, scale, sms, st, cos_t, sin_t);
 }
