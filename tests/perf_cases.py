@@ -7,11 +7,13 @@ Also the small, self-contained cases used for ncu captures.
 CASE: decode (config 2: 64 takes, slots of 4096, lengths U[330,4096]; per layer)
       step (config 2 per layer: decode prologue + attention, programmatic dependent launch unless --pdl 0)
       decode1 (config 1: one take, 512 of 4096 positions)
-      prefill (config 3: T = 1024 causal, 16 q / 2 kv heads, hd 128; per layer)
+      prefill (config 3: T = 1024 causal, 16 q / 2 kv heads, hd 128; per layer; --T for other prompt lengths)
       replicate (config 3: the prompt KV of one layer, K and V, into 64 slots of 4096)
       prefill_kv (config 3 per layer in one launch: prefill + k/v into all 64 slots; and the separate launches)
       locdit (config 4: 512 sequences x 12 tokens, 16 heads, hd 64)
       locdit_ref (the reference's DiT shape: 512 sequences x 11 tokens, 16 q / 2 kv heads, hd 128)
+      locdit_ref_rope (the same with the rope: one launch for ours, rope then attention for the reference)
+      locenc (the local encoder at 256 takes: 256 sequences x 5 tokens, 16 q / 2 kv heads, hd 128, rope)
       loop (config 5 decoding loop, 32 takes, --reps steps: host loop reading the stop flags after every replay
             against the same graph inside one launch with the stop test on the device; per step)
 Prints one JSON line: mean milliseconds per launch (CUDA events on the launching stream, after warm-up) and the
@@ -215,15 +217,23 @@ def case_prefill_kv(args, B=64, maxlen=4096, T=1024):
                 kv_bytes_written=2 * B * NK * T * HD * 2)
 
 
-def case_small(args, impl, nseq, seq, nq, nk, hd):
+def case_small(args, impl, nseq, seq, nq, nk, hd, rope=False):
     rows, W = nseq * seq, (nq + 2 * nk) * hd
     layers = max(args.layers, 8)  # rotate inputs so consecutive calls do not hit L2
     qkv = [rnd((rows, W), 500 + l) for l in range(layers)]
     out = torch.zeros((rows, nq * hd), dtype=torch.bfloat16, device="cuda")
     nbytes = rows * (nq + 2 * nk) * hd * 2 + rows * nq * hd * 2
     K = ops if impl == "ours" else __import__("oracle.refkern", fromlist=["x"])
+    if rope:
+        from oracle import cpu  # the reference builds its rotary tables on the host (src/model.rs:337-349)
+        cs, sn = (torch.from_numpy(t).cuda() for t in cpu.rotary_tables(seq, hd))
 
     def fn(i):
+        if rope and impl == "ours":  # one launch: rope + attention (Engine::full's DiT call)
+            K.attn_full_rope(qkv[i % layers], out, cs, sn, rows, seq, 0, nq, nk, hd, hd ** -0.5)
+            return
+        if rope:  # the reference's two launches; q and k are rotated again on each call (timing only)
+            K.rope(qkv[i % layers], cs, sn, None, rows, seq, nq, nk, hd)
         K.attn_full(qkv[i % layers], out, rows, seq, 0, nq, nk, hd, hd ** -0.5)
     ms = timed(fn, args.reps, args.warmup)
     return dict(ms=ms, bytes=nbytes, GBps=nbytes / ms / 1e6)
@@ -238,6 +248,7 @@ def main():
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--eager", action="store_true", help="time calls one by one instead of graph replay")
     ap.add_argument("--pdl", type=int, default=1, help="step case: programmatic dependent launch on/off")
+    ap.add_argument("--T", type=int, default=1024, help="prefill case: prompt length")
     args = ap.parse_args()
     global GRAPH
     GRAPH = not args.eager
@@ -255,7 +266,7 @@ def main():
     elif c == "decode1":
         r = case_decode(args, args.impl, [512])
     elif c == "prefill":
-        r = case_prefill(args, args.impl)
+        r = case_prefill(args, args.impl, T=args.T)
     elif c == "replicate":
         r = case_replicate(args, args.impl)
     elif c == "prefill_kv":
@@ -266,6 +277,10 @@ def main():
         r = case_small(args, args.impl, 512, 12, 16, 16, 64)
     elif c == "locdit_ref":
         r = case_small(args, args.impl, 512, 11, 16, 2, 128)
+    elif c == "locdit_ref_rope":
+        r = case_small(args, args.impl, 512, 11, 16, 2, 128, rope=True)
+    elif c == "locenc":
+        r = case_small(args, args.impl, 256, 5, 16, 2, 128, rope=True)
     else:
         raise SystemExit(f"unknown case {c}")
     r.update(case=c, impl=args.impl, reps=args.reps)
