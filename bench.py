@@ -521,6 +521,17 @@ def main():
     torch.cuda.synchronize()
     e2e_ms_local = f0.elapsed_time(f1)
     e2e_ms = max_over_ranks(e2e_ms_local)
+    # the same loop serialised on one stream (copy in, step, copy out, in order), for comparison
+    barrier()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(s_comp)
+    for _ in range(args.steps):
+        qkv_b[0].copy_(qkv_host, non_blocking=True)
+        graphs[0].replay()
+        att_host.copy_(att_b[0], non_blocking=True)
+    g1.record(s_comp)
+    torch.cuda.synchronize()
+    e2e_serial_ms = max_over_ranks(g0.elapsed_time(g1))
     del graph2
     e2e_value = total_bytes / (e2e_ms / 1e3) / 1e9
     errword = ops.device_error()
@@ -557,6 +568,8 @@ def main():
                          "algorithmic_bytes_per_launch": per_layer},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / args.steps, 4),
+                    "serialised_value": round(total_bytes / (e2e_serial_ms / 1e3) / 1e9, 2),
+                    "serialised_ms_per_step": round(e2e_serial_ms / args.steps, 4),
                     "path": "pinned host qkv -> device, graph of C-ABI calls, attention output -> pinned host; "
                             "double-buffered: the copies of neighbouring steps overlap a step's compute"},
             "cpu_baseline": cpu_base,
