@@ -9,7 +9,8 @@ written into the take's slot, and the split-KV decode attention with the combine
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 For N > 1 it runs under torchrun, one rank per GPU; every rank owns its own 64 takes (takes are independent,
-no collective on the data path), so scaling is weak. Rank 0 prints one JSON line.
+no collective on the data path), so scaling is weak: N x 64 lengths are drawn from the seed and dealt out so that
+every GPU holds about the same KV bytes. Rank 0 prints one JSON line.
 --impl reference times the reference algorithm's CPU restatement (oracle/, all host threads) on the same workload.
 """
 import argparse
@@ -52,9 +53,25 @@ def emit(line):
     os.write(_STDOUT_FD if _STDOUT_FD is not None else 1, data)
 
 
-def take_lengths(rank):
+def shard_lengths(seed, per_rank, world, rank, lo, hi):
+    """This rank's per_rank take lengths: world * per_rank lengths drawn from the seed (the first per_rank of them are
+    the one-GPU draw), dealt out longest first to the rank with the fewest cached positions so far, each rank taking
+    per_rank takes, as a host placing takes on GPUs balances their KV bytes. Kept in draw order. (Independent draws
+    per rank differed by up to 18 % in bytes, and the max-over-ranks time then measured that imbalance.)"""
     from oumu_b200 import synth
-    return synth.uniform_int(synth.config_seed(1) + 1000 * rank, TAKES, LEN_LO, LEN_HI)
+    allv = [int(v) for v in synth.uniform_int(seed, world * per_rank, lo, hi)]
+    if world == 1:
+        return allv
+    load, mine = [0] * world, [[] for _ in range(world)]
+    for i in sorted(range(len(allv)), key=lambda i: (-allv[i], i)):
+        r = min((q for q in range(world) if len(mine[q]) < per_rank), key=lambda q: (load[q], q))
+        mine[r].append(i)
+        load[r] += allv[i]
+    return [allv[i] for i in sorted(mine[rank])]
+
+
+def take_lengths(rank, world=1):
+    return shard_lengths(0x5EED + 1, TAKES, world, rank, LEN_LO, LEN_HI)
 
 
 def bytes_per_layer(lens):
@@ -267,7 +284,7 @@ def patches_leg(args, dev, rank, max_over_ranks, sum_over_ranks, barrier, world=
     from oumu_b200 import engine, synth
     B, K, W = args.step_takes, args.step_steps, max(3, min(args.warmup, 5))
     margin = 2 * (K + W) + 4  # every replay advances every take by one position; lengths reset between legs
-    lens = synth.uniform_int(synth.config_seed(5) + 1000 * rank, B, LEN_LO, MAXLEN - margin)
+    lens = shard_lengths(synth.config_seed(5), B, world, rank, LEN_LO, MAXLEN - margin)
     e = engine.Engine(B, maxlen=MAXLEN, max_steps=4 * (K + W) + 8, device=dev)
     e.prime(lens, seed=5 + rank)
     from oumu_b200 import _lib
@@ -365,7 +382,7 @@ def main():
         build.build()
     if world > 1:
         dist.barrier()
-    lens = take_lengths(rank)
+    lens = take_lengths(rank, world)
     W = (NQ + 2 * NK) * HD
     gen = torch.Generator(device=dev)
     gen.manual_seed(0x5EED + 1 + rank)
