@@ -1,5 +1,6 @@
-"""The multi-GPU plumbing of bench.py on CPU ranks (gloo, world size 2): each rank owns its own takes (disjoint,
-seeded per rank, no collective on the data path) and rank 0 reports the summed bytes over the max device time."""
+"""The multi-GPU plumbing of bench.py on CPU ranks (gloo, world size 2): each rank owns its own takes (disjoint
+shares of one seeded draw, balanced in KV bytes, no collective on the data path) and rank 0 reports the summed
+bytes over the max device time."""
 import os
 import sys
 from datetime import timedelta
@@ -16,7 +17,7 @@ def _worker(rank, world, port, q):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=timedelta(seconds=60))
     try:
-        lens = bench.take_lengths(rank)
+        lens = bench.take_lengths(rank, world)
         per_step = bench.LAYERS * bench.bytes_per_layer(lens)
         ms = 10.0 + 3.0 * rank  # each rank's own (pretend) device time
         total = bench.rank_reduce(per_step, "sum", dist)
@@ -43,6 +44,9 @@ def test_two_ranks_shard_takes_and_aggregate():
     (_, l0, b0, t0, m0), (_, l1, b1, t1, m1) = res[0], res[1]
     assert len(l0) == len(l1) == 64 and l0 != l1             # each rank its own 64 takes
     assert all(330 <= x <= 4096 for x in l0 + l1)
+    from oumu_b200 import synth                              # together: the seeded draw of 128 takes, dealt out
+    assert sorted(l0 + l1) == sorted(int(v) for v in synth.uniform_int(0x5EED + 1, 128, 330, 4096))
+    assert abs(sum(l0) - sum(l1)) <= 4096                    # balanced to within one take's length
     assert t0 == t1 == b0 + b1                               # bytes of all ranks
     assert m0 == m1 == 13.0                                  # the slowest rank's time
 
