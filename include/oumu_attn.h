@@ -41,14 +41,16 @@ const char *oumu_status_string(int status);
 const char *oumu_last_cuda_error(void);
 
 /*
- * Programmatic dependent launch for the decode kernels (oumu_decode_prologue, oumu_attn_decode,
- * oumu_attn_decode_step), process-wide,
- * off by default; returns the previous setting. When on, these kernels are launched so that they may start while
- * the preceding kernel in the stream is still running: their set-up, and the loads of cache positions below each
- * take's newest position, overlap it; q, the newest position and every global write wait for it to complete. The
- * caller guarantees that the preceding kernels of the same step do not write `pos`/`lens` or cache positions below
- * the newest one (true of the reference's step, where ctr advances only in step_end, src/model.rs:771, and
- * kv_write writes only position *pos, src/model.rs:590-595). Captured into CUDA graphs as programmatic edges.
+ * Programmatic dependent launch, process-wide, off by default; returns the previous setting. Applies to the decode
+ * kernels (oumu_decode_prologue, oumu_attn_decode, oumu_attn_decode_step), oumu_gemm and the glue kernels
+ * oumu_rmsnorm, oumu_silu_mul and oumu_pointwise (include/oumu_step.h). When on, these kernels are launched so that
+ * they may start while the preceding kernel in the stream is still running, and each lets its successor start at
+ * once: their set-up and their reads of constant data (GEMM weights, norm weights, cache positions below each take's
+ * newest position) overlap the preceding kernel; everything it may write (q, activations, the newest position) is
+ * read, and every global write made, only after it has completed. The caller guarantees that the preceding kernels
+ * of the same step do not write `pos`/`lens`, cache positions below the newest one, or weights (true of the
+ * reference's step, where ctr advances only in step_end, src/model.rs:771, and kv_write writes only position *pos,
+ * src/model.rs:590-595). Captured into CUDA graphs as programmatic edges.
  */
 int oumu_set_pdl(int enable);
 

@@ -838,15 +838,15 @@ int oumu_rmsnorm(void *res, const void *d, const void *w, void *out, int rows, i
     if (!aligned16(res) || !aligned16(w) || !aligned16(out) || (d && !aligned16(d))) return OUMU_ERR_INVALID;
     if (rows == 0) return OUMU_OK;
     const unsigned grid = static_cast<unsigned>(rows);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (dim == 1024)
-        glue::k_rmsnorm<1024><<<grid, 128, 0, stream>>>(static_cast<bf16 *>(res), static_cast<const bf16 *>(d),
-                                                        static_cast<const bf16 *>(w), static_cast<bf16 *>(out), rows,
-                                                        eps);
+        OUMU_CK(launch_k(glue::k_rmsnorm<1024>, dim3(grid), dim3(128), 0, st, static_cast<bf16 *>(res),
+                         static_cast<const bf16 *>(d), static_cast<const bf16 *>(w), static_cast<bf16 *>(out), rows,
+                         eps));
     else
-        glue::k_rmsnorm<2048><<<grid, 256, 0, stream>>>(static_cast<bf16 *>(res), static_cast<const bf16 *>(d),
-                                                        static_cast<const bf16 *>(w), static_cast<bf16 *>(out), rows,
-                                                        eps);
-    OUMU_CK(cudaGetLastError());
+        OUMU_CK(launch_k(glue::k_rmsnorm<2048>, dim3(grid), dim3(256), 0, st, static_cast<bf16 *>(res),
+                         static_cast<const bf16 *>(d), static_cast<const bf16 *>(w), static_cast<bf16 *>(out), rows,
+                         eps));
     return OUMU_OK;
 }
 
@@ -855,9 +855,9 @@ int oumu_silu_mul(const void *gu, void *out, int rows, int F, oumu_stream_t stre
     if (!aligned16(gu) || !aligned16(out)) return OUMU_ERR_INVALID;
     const long vecs = static_cast<long>(rows) * (F / 8);
     if (vecs == 0) return OUMU_OK;
-    glue::k_silu_mul<<<static_cast<unsigned>((vecs + 255) / 256), 256, 0, stream>>>(
-        static_cast<const bf16 *>(gu), static_cast<bf16 *>(out), rows, F);
-    OUMU_CK(cudaGetLastError());
+    OUMU_CK(launch_k(glue::k_silu_mul, dim3(static_cast<unsigned>((vecs + 255) / 256)), dim3(256), 0,
+                     reinterpret_cast<cudaStream_t>(stream), static_cast<const bf16 *>(gu), static_cast<bf16 *>(out),
+                     rows, F));
     return OUMU_OK;
 }
 
@@ -866,9 +866,8 @@ int oumu_pointwise(void *x, long n, int op, float scale, oumu_stream_t stream) {
     if (op == 1 && !(scale != 0.f)) return OUMU_ERR_INVALID;
     if (n == 0) return OUMU_OK;
     const long vecs = n / 8;
-    glue::k_pointwise<<<static_cast<unsigned>((vecs + 255) / 256), 256, 0, stream>>>(static_cast<bf16 *>(x), n, op,
-                                                                                     scale);
-    OUMU_CK(cudaGetLastError());
+    OUMU_CK(launch_k(glue::k_pointwise, dim3(static_cast<unsigned>((vecs + 255) / 256)), dim3(256), 0,
+                     reinterpret_cast<cudaStream_t>(stream), static_cast<bf16 *>(x), n, op, scale));
     return OUMU_OK;
 }
 

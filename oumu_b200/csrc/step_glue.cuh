@@ -1,6 +1,7 @@
 // Element-wise and per-row kernels of the decoding step around the attention (the step's glue): RMS norms, the
 // SwiGLU product, the DiT and local-encoder input sequences, classifier-free guidance with the Euler update, the
-// FSQ activation and the step end. Each has the rounding points of the reference kernel it stands in for
+// FSQ activation and the step end. The norm, SwiGLU and pointwise kernels take part in programmatic dependent launch
+// (oumu_set_pdl): they let the next kernel start at once and wait for the preceding one before touching its outputs. Each has the rounding points of the reference kernel it stands in for
 // (kernels/voxcpm.cu), so a step built from them tracks the reference step; the layouts are this library's own:
 // every kernel moves 16-byte vectors, and row norms run one block per row with the row held in registers.
 #pragma once
@@ -48,8 +49,10 @@ __global__ void __launch_bounds__(DIM / 8) k_rmsnorm(bf16 *res, const bf16 *d, c
     const long row = blockIdx.x;
     bf16 *xr = res + row * DIM;
     float v[8], wv[8];
+    pdl_trigger();
+    load8(w + c, wv);  // the norm weights are constant: read before the preceding kernel has finished
+    pdl_wait();
     load8(xr + c, v);
-    load8(w + c, wv);
     if (d) {
         float dv[8];
         load8(d + row * DIM + c, dv);
@@ -75,6 +78,8 @@ __global__ void __launch_bounds__(DIM / 8) k_rmsnorm(bf16 *res, const bf16 *d, c
 
 // out[r, c] = bf16(bf16(silu(gate)) * up) with gu = [gate | up] per row, F columns each (kernels/voxcpm.cu:92-99).
 __global__ void __launch_bounds__(256) k_silu_mul(const bf16 *gu, bf16 *out, int rows, int F) {
+    pdl_trigger();
+    pdl_wait();
     const long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;  // vector index
     const int fv = F / 8;
     if (i >= static_cast<long>(rows) * fv) return;
@@ -91,6 +96,8 @@ __global__ void __launch_bounds__(256) k_silu_mul(const bf16 *gu, bf16 *out, int
 // In place over n elements (n % 8 == 0): op 0 = silu (kernels/voxcpm.cu:80-83); op 1 = FSQ,
 // h = bf16(rint(bf16(bf16(tanh(h)) * scale)) / scale) (kernels/voxcpm.cu:370-375).
 __global__ void __launch_bounds__(256) k_pointwise(bf16 *x, long n, int op, float scale) {
+    pdl_trigger();
+    pdl_wait();
     const long i = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
     if (i >= n) return;
     float v[8];

@@ -5,9 +5,10 @@ DiT passes with classifier-free guidance (src/model.rs:733-749) -> local encoder
 head (:754-756) -> base LM step (:758) -> FSQ -> fusion -> residual LM step (:759-764) -> step end (:766-772).
 Every kernel outside the GEMMs is this library's, through the C ABI: the fused decode layer of the LMs
 (oumu_attn_decode_step), the small-sequence attention of the DiT and the local encoder (oumu_attn_full) with its
-rope, and the step glue of include/oumu_step.h. GEMMs are cuBLAS through torch (bf16 in and out, fp32 accumulate,
-bias added in the epilogue and rounded once, as the reference's gemm_ex with beta = 1 over a bias-filled output,
-src/gpu.rs:186-229, kernels/voxcpm.cu:70-76).
+rope, and the step glue of include/oumu_step.h. The LM projections (qkv, o, gate|up, down at 1 row per take) run
+on this library's tcgen05 GEMM (oumu_gemm); the DiT's and the heads' GEMMs are cuBLAS through torch (bf16 in and
+out, fp32 accumulate, bias added in the epilogue and rounded once, as the reference's gemm_ex with beta = 1 over a
+bias-filled output, src/gpu.rs:186-229, kernels/voxcpm.cu:70-76).
 
 Weights are random (seeded N(0, 0.02) bf16; norm weights 1 + N(0, 0.02)) and the KV slots hold random prompt
 state: the step is for timing, not for audio. The whole step is captured as one CUDA graph and replayed, the
@@ -134,9 +135,11 @@ class Tf:
 class Engine:
     """Weights, KV slots and step buffers for B takes (src/model.rs:184-243, 404-529)."""
 
-    # LM projections that run on this library's GEMM (oumu_gemm) instead of cuBLAS: none by default; inside the
-    # captured step cuBLAS measured 4.75 ms against 4.79 ms with o and down on oumu_gemm (32 takes, B200)
-    LM_TC = ()
+    # LM projections that run on this library's GEMM (oumu_gemm) instead of cuBLAS: all four by default. With
+    # programmatic dependent launch through the norm / SwiGLU kernels between them, each GEMM streams its weights
+    # while the preceding kernel finishes: 4.68 ms per captured step against 4.77 ms on cuBLAS (32 takes, the same
+    # B200). lm_tc=() selects cuBLAS.
+    LM_TC = ("qkv", "o", "gu", "down")
 
     def __init__(self, B, maxlen=4096, timesteps=10, base_layers=28, res_layers=8, enc_layers=4, dit_layers=4,
                  cfg=2.0, max_steps=256, min_len=2, seed=0, device="cuda", lm_tc=LM_TC):

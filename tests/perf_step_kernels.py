@@ -1,7 +1,7 @@
 """Per-kernel device time of one decoding step of config 5 (oumu_b200.engine.Engine, captured as one CUDA graph):
 the kernels a step launches, how often, and their share of the step.
 
-    python tests/perf_step_kernels.py [--takes 32] [--steps 3]
+    python tests/perf_step_kernels.py [--takes 32] [--steps 3] [--lm-tc qkv,o,gu,down]
         torch profiler (CUDA activity) over `steps` graph replays: one line per kernel name.
     ncu --profile-from-start off --metrics gpu__time_duration.sum --clock-control none --csv \\
         --log-file launches.csv python tests/perf_step_kernels.py --ncu
@@ -25,9 +25,11 @@ def main():
     ap.add_argument("--takes", type=int, default=32)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--ncu", action="store_true", help="one replay inside cudaProfilerStart/Stop, nothing printed")
+    ap.add_argument("--lm-tc", default=None, help="LM projections on the library's GEMM (comma list; 'none': cuBLAS)")
     args = ap.parse_args()
     B = args.takes
-    e = engine.Engine(B)
+    kw = {} if args.lm_tc is None else {"lm_tc": () if args.lm_tc == "none" else tuple(args.lm_tc.split(","))}
+    e = engine.Engine(B, **kw)
     margin = 2 * (args.steps + 8)
     e.prime([int(v) for v in synth.uniform_int(synth.config_seed(5), B, 330, 4096 - margin)])
     g = e.capture()

@@ -2,7 +2,7 @@
 src/model.rs:725-773) against the same step run through the reference's own kernels (tests/perf_step_ref.py:
 rmsnorm, rope, kv_write, attn_decode + attn_combine, attn_full, dit_build, gather_rows, cfg_euler, fsq_act, step_end
 ... from kernels/voxcpm.cu, launched with the grids of src/model.rs), on the same weights, KV state and diffusion
-noise, with cuBLAS GEMMs in both.
+noise; the reference side's GEMMs are cuBLAS, ours cuBLAS or this library's GEMM for the LM projections.
 
 The reference decodes every take at one shared position (src/model.rs:596-615), so the takes share one length. The
 noise is the reference's verification mode (a replayed [step][64][4] table, kernels/voxcpm.cu:347-366) on its side
@@ -55,14 +55,15 @@ def _load_state(dst, src):
         getattr(dst, name).copy_(getattr(src, name))
 
 
-def test_decoding_step_matches_the_reference_kernels(cuda):
+@pytest.mark.parametrize("lm_tc", [(), ("qkv", "o", "gu", "down")], ids=["cublas_gemms", "library_gemms"])
+def test_decoding_step_matches_the_reference_kernels(cuda, lm_tc):
     from oracle import refkern
     if not refkern.available():
         pytest.skip("oracle/_ref/voxcpm_ref.fatbin not built (needs the reference tree)")
     import perf_step_ref
 
     kw = dict(maxlen=MAXLEN, max_steps=16, min_len=2, seed=0)
-    ours = _probe(engine.Engine)(B, **kw)
+    ours = _probe(engine.Engine)(B, lm_tc=lm_tc, **kw)
     ref = _probe(perf_step_ref.RefStep)(B, **kw)
     pert = _probe(perf_step_ref.RefStep)(B, **kw)
     ref.prime([L0] * B, seed=1)
