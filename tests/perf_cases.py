@@ -44,6 +44,7 @@ def rnd(shape, seed):
 
 
 GRAPH = True
+PROFILE = False
 
 
 def timed(fn, reps, warmup):
@@ -73,10 +74,14 @@ def timed(fn, reps, warmup):
     g.replay()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if PROFILE:  # only the timed replay between cudaProfilerStart / Stop (ncu --profile-from-start off)
+        torch.cuda.profiler.start()
     a.record()
     g.replay()
     b.record()
     torch.cuda.synchronize()
+    if PROFILE:
+        torch.cuda.profiler.stop()
     del g
     return a.elapsed_time(b) / reps
 
@@ -249,9 +254,12 @@ def main():
     ap.add_argument("--eager", action="store_true", help="time calls one by one instead of graph replay")
     ap.add_argument("--pdl", type=int, default=1, help="step case: programmatic dependent launch on/off")
     ap.add_argument("--T", type=int, default=1024, help="prefill case: prompt length")
+    ap.add_argument("--profile", action="store_true",
+                    help="bracket the timed graph replay with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     args = ap.parse_args()
-    global GRAPH
+    global GRAPH, PROFILE
     GRAPH = not args.eager
+    PROFILE = args.profile
     if args.impl == "ours":
         from oumu_b200 import build
         build.build()
