@@ -285,6 +285,12 @@ __global__ void __launch_bounds__(nthreads(NWG), 1)
                 }
                 tc_commit(bar(B_S + w));
                 s_issued = j;
+                // while S runs: the previous unit's output stores have read their slot, which goes back to the
+                // producer (nothing waits for it on the unit's own chain)
+                if (k >= w + NWG) {
+                    bulk_wait_read();
+                    mbar_arrive(bar(B_EMPTY + (k - NWG) % P.nslot));
+                }
             }
             __syncwarp();
             // ---- softmax of row m: S from TMEM, P (bf16 hi + lo) back into the same columns ----
@@ -351,14 +357,18 @@ __global__ void __launch_bounds__(nthreads(NWG), 1)
             ok = __all_sync(0xffffffffu, mbar_wait(bar(B_O + w), j & 1));
             if (ok) {
                 tc_fence_after();
+                // two loads in flight per wait, except in the rope build (which would spill at 128 registers)
+                constexpr int OB = ROPE ? 32 : 64;
 #pragma unroll
-                for (int cb = 0; cb < HD; cb += 32) {
-                    uint32_t o[32];
+                for (int cb = 0; cb < HD; cb += OB) {
+                    uint32_t o[OB];
                     tmem_ld32(tO + cb, o);
+                    if (OB == 64 && cb + 32 < HD) tmem_ld32(tO + cb + 32, o + OB - 32);
                     tc_wait_ld();
                     if (m < P.qrows) {
 #pragma unroll
-                        for (int q = 0; q < 4; q++) {
+                        for (int q = 0; q < OB / 8; q++) {
+                            if (cb + q * 8 >= HD) break;
                             uint4 v;
                             v.x = pack_bf16x2(__uint_as_float(o[8 * q]) * inv, __uint_as_float(o[8 * q + 1]) * inv);
                             v.y = pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv);
@@ -378,12 +388,11 @@ __global__ void __launch_bounds__(nthreads(NWG), 1)
                 unit_heads(P, c + k * grid, n, qh0, kh0);
 #pragma unroll
                 for (int b = 0; b < NBOX; b++) tma_store_3d(&tout, base + b * P.qbox, b * 64, qh0, n * P.seq);
-                bulk_commit();
-                bulk_wait_read();  // the slot may be reloaded once the stores have read it
-                mbar_arrive(bar(B_EMPTY + k % P.nslot));
+                bulk_commit();  // the slot goes back to the producer at the next unit, once the stores have read it
             }
             __syncwarp();
         }
+        if (wtid == 0) bulk_wait_read();  // every store has read its slot before the CTA may leave
         if (!ok && wtid == 0) {
             *abort_flag = 1;
             // nothing may still write TMEM when it is freed: wait (bounded) for the last MMAs issued
