@@ -401,9 +401,9 @@ int launch_prefill(const void *qkv, void *out, int rows, int seq, int causal, in
         rc = make_map_cache(&tvc, vc, HD, seq, slots * nk, maxlen, pf::BN);
         if (rc) return rc;
     }
-    const int nseq = rows / seq;
-    if (nseq > 65535 || nq > 65535) return OUMU_ERR_UNSUPPORTED;
-    dim3 grid((seq + pf::BM - 1) / pf::BM, nq, nseq);
+    const int nseq = rows / seq, qtiles = (seq + pf::BM - 1) / pf::BM;
+    if (nseq > 65535 || qtiles > 65535) return OUMU_ERR_UNSUPPORTED;
+    dim3 grid(nq, qtiles, nseq);
     pf::k_attn_prefill<HD><<<grid, pf::NTHREADS, pf::Cfg<HD>::SMEM, st>>>(
         tm, static_cast<bf16 *>(out), seq, causal, nq, nk, scale * 1.4426950408889634f, tkc, tvc, slots);
     OUMU_CK(cudaGetLastError());

@@ -1,7 +1,7 @@
 // Flash attention on the 5th-generation tensor cores (tcgen05 + TMEM), fed by TMA, for long sequences: the causal
 // prefill over the prompt (src/model.rs:688,701 -> full(..., causal = true)).
 //
-// One CTA per (128-query tile, q head, sequence). Warp roles:
+// One CTA per (q head, 128-query tile, sequence), heaviest tiles first. Warp roles:
 //   warp 0      TMA producer: Q tile once, then K and V tiles of 128 positions into two 2-stage rings: a K stage is
 //               free again once its S = Q.K^T has completed, a V stage once its P.V has, so the K of tile j+2
 //               loads while P_j.V still runs (the V loads trail the K loads by one tile)
@@ -72,8 +72,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + C::BAR_OFF + 8 * B_ABORT);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qt = gridDim.x - 1 - blockIdx.x;  // heaviest causal tiles first
-    const int h = blockIdx.y, n = blockIdx.z, G = nq / nk, kh = h / G;
+    // CTAs start in block order, x fastest: every head's heaviest causal tile first, then the next heaviest, ... so
+    // that the tiles left for the last wave are the short ones
+    const int qt = gridDim.y - 1 - blockIdx.y;
+    const int h = blockIdx.x, n = blockIdx.z, G = nq / nk, kh = h / G;
     const int q0 = qt * BM;
     const int row0 = n * seq;  // first row of this sequence in qkv
     const int ntiles_all = (seq + BN - 1) / BN;
