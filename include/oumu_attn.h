@@ -42,12 +42,15 @@ const char *oumu_last_cuda_error(void);
 
 /*
  * Programmatic dependent launch, process-wide, off by default; returns the previous setting. Applies to the decode
- * kernels (oumu_decode_prologue, oumu_attn_decode, oumu_attn_decode_step), oumu_gemm and the glue kernels
- * oumu_rmsnorm, oumu_silu_mul and oumu_pointwise (include/oumu_step.h). When on, these kernels are launched so that
- * they may start while the preceding kernel in the stream is still running, and each lets its successor start at
- * once: their set-up and their reads of constant data (GEMM weights, norm weights, cache positions below each take's
- * newest position) overlap the preceding kernel; everything it may write (q, activations, the newest position) is
- * read, and every global write made, only after it has completed. The caller guarantees that the preceding kernels
+ * kernels (oumu_decode_prologue, oumu_attn_decode, oumu_attn_decode_step), oumu_gemm, the glue kernels
+ * oumu_rmsnorm, oumu_silu_mul and oumu_pointwise (include/oumu_step.h), and the tensor-memory attention kernels of
+ * oumu_attn_full, oumu_attn_full_rope and oumu_attn_prefill_kv (causal prefill, short sequences). When on, these
+ * kernels are launched so that they may start while the preceding kernel in the stream is still running: their
+ * set-up and their reads of constant data (GEMM weights, norm weights, cache positions below each take's newest
+ * position) overlap the preceding kernel; everything it may write (q, activations, the newest position) is read,
+ * and every global write made, only after it has completed. Most let their successor start at once; the attention
+ * kernels that hold all of an SM's tensor memory take it only after the preceding kernel has completed and let
+ * their successor in only once they hold it. The caller guarantees that the preceding kernels
  * of the same step do not write `pos`/`lens`, cache positions below the newest one, or weights (true of the
  * reference's step, where ctr advances only in step_end, src/model.rs:771, and kv_write writes only position *pos,
  * src/model.rs:590-595). Captured into CUDA graphs as programmatic edges.

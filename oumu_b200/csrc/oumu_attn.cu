@@ -377,11 +377,11 @@ int launch_small_tc(const void *qkv, void *out, int rows, int seq, int causal, i
     const int smem = std::max(sq::smem_bytes(P.slot, P.nslot), 120 * 1024);
     if (KS == 1) {
         auto kern = cos_t ? sq::k_attn_small_tc<HD, 16, 3, true> : sq::k_attn_small_tc<HD, 16, 3, false>;
-        kern<<<grid, sq::nthreads(3), smem, st>>>(tq, tkv, tout, P);
+        OUMU_CK(launch_k(kern, dim3(grid), dim3(sq::nthreads(3)), smem, st, tq, tkv, tout, P));
     } else {
-        sq::k_attn_small_tc<HD, 128, 2, false><<<grid, sq::nthreads(2), smem, st>>>(tq, tkv, tout, P);
+        OUMU_CK(launch_k(sq::k_attn_small_tc<HD, 128, 2, false>, dim3(grid), dim3(sq::nthreads(2)), smem, st, tq,
+                         tkv, tout, P));
     }
-    OUMU_CK(cudaGetLastError());
     return OUMU_OK;
 }
 
@@ -404,9 +404,8 @@ int launch_prefill(const void *qkv, void *out, int rows, int seq, int causal, in
     const int nseq = rows / seq, qtiles = (seq + pf::BM - 1) / pf::BM;
     if (nseq > 65535 || qtiles > 65535) return OUMU_ERR_UNSUPPORTED;
     dim3 grid(nq, qtiles, nseq);
-    pf::k_attn_prefill<HD><<<grid, pf::NTHREADS, pf::Cfg<HD>::SMEM, st>>>(
-        tm, static_cast<bf16 *>(out), seq, causal, nq, nk, scale * 1.4426950408889634f, tkc, tvc, slots);
-    OUMU_CK(cudaGetLastError());
+    OUMU_CK(launch_k(pf::k_attn_prefill<HD>, grid, dim3(pf::NTHREADS), pf::Cfg<HD>::SMEM, st, tm,
+                     static_cast<bf16 *>(out), seq, causal, nq, nk, scale * 1.4426950408889634f, tkc, tvc, slots));
     return OUMU_OK;
 }
 

@@ -101,7 +101,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         *abort_flag = 0;
         mbar_fence_init();
     }
+    // Programmatic dependent launch: the set-up above overlaps the preceding kernel; TMEM is allocated only after it
+    // has completed (a kernel that takes all 512 columns before its predecessor ends could hold columns that
+    // predecessor has yet to allocate), and the next kernel is let in only once the columns are held.
     if (warp == 1) {
+        pdl_wait();
         tmem_alloc(bar(B_TMEM), C::TMEM_COLS);
         tmem_relinquish();
     }
@@ -109,6 +113,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (threadIdx.x == 0) pdl_trigger();
 
     if (warp == 0) {
         // ------------------------------ TMA producer ------------------------------

@@ -139,7 +139,12 @@ __global__ void __launch_bounds__(nthreads(NWG), 1)
         *abort_flag = 0;
         mbar_fence_init();
     }
+    // Programmatic dependent launch: the set-up above and the padding below overlap the preceding kernel; TMEM is
+    // allocated only after it has completed (a kernel that takes all 512 columns before its predecessor ends could
+    // hold columns that predecessor has yet to allocate), and the next kernel is let in only once the columns are
+    // held (so none of its CTAs can take them first).
     if (warp == 0) {
+        pdl_wait();
         tmem_alloc(bar(B_TMEM), 512);
         tmem_relinquish();
     }
@@ -160,6 +165,7 @@ __global__ void __launch_bounds__(nthreads(NWG), 1)
     float *tab_c = reinterpret_cast<float *>(sm + bar_off + BAR_BYTES);
     float *tab_s = tab_c + TAB_BYTES / 8;
     if (ROPE) {
+        pdl_wait();  // the tables are read after the preceding kernel like every other input
         for (int i = threadIdx.x; i < P.seq * (HD / 2); i += nthreads(NWG)) {
             tab_c[i] = P.cos_t[i];
             tab_s[i] = P.sin_t[i];
@@ -169,6 +175,7 @@ __global__ void __launch_bounds__(nthreads(NWG), 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (threadIdx.x == 0) pdl_trigger();
 
     int last_k[NSLOT_MAX];  // producer: the last unit loaded into each slot (-1: none)
     if (warp == 0) {

@@ -5,7 +5,7 @@ Also the small, self-contained cases used for ncu captures.
     python tests/perf_cases.py CASE [--impl ours|ref] [--reps N] [--warmup N] [--layers N]
 
 CASE: decode (config 2: 64 takes, slots of 4096, lengths U[330,4096]; per layer)
-      step (config 2 per layer: decode prologue + attention, programmatic dependent launch unless --pdl 0)
+      step (config 2 per layer: decode prologue + attention)
       decode1 (config 1: one take, 512 of 4096 positions)
       prefill (config 3: T = 1024 causal, 16 q / 2 kv heads, hd 128; per layer; --T for other prompt lengths)
       replicate (config 3: the prompt KV of one layer, K and V, into 64 slots of 4096)
@@ -16,7 +16,8 @@ CASE: decode (config 2: 64 takes, slots of 4096, lengths U[330,4096]; per layer)
       locenc (the local encoder at 256 takes: 256 sequences x 5 tokens, 16 q / 2 kv heads, hd 128, rope)
       loop (config 5 decoding loop, 32 takes, --reps steps: host loop reading the stop flags after every replay
             against the same graph inside one launch with the stop test on the device; per step)
-Prints one JSON line: mean milliseconds per launch (CUDA events on the launching stream, after warm-up) and the
+The step, prefill and short-sequence cases launch this library's kernels with programmatic dependent launch unless
+--pdl 0. Prints one JSON line: mean milliseconds per launch (CUDA events on the launching stream, after warm-up) and the
 algorithmic bytes / FLOPs per launch. With --impl ref and per-take lengths, the reference kernel (one shared
 position) runs once per take with slot-offset pointers; "decode_shared" instead runs every take at the mean length.
 """
@@ -183,8 +184,8 @@ def case_prefill(args, impl, T=1024):
 
     def fn(i):
         K.attn_full(qkv[i % layers], out, T, T, 1, NQ, NK, HD, HD ** -0.5)
-    ms = timed(fn, args.reps, args.warmup)
-    return dict(ms=ms, flops=flops, TFLOPs=flops / ms / 1e9)
+    ms = timed_pdl(fn, args, impl)
+    return dict(ms=ms, flops=flops, TFLOPs=flops / ms / 1e9, pdl=args.pdl if impl == "ours" else 0)
 
 
 def case_replicate(args, impl, B=64, maxlen=4096, T=1024):
@@ -222,6 +223,17 @@ def case_prefill_kv(args, B=64, maxlen=4096, T=1024):
                 kv_bytes_written=2 * B * NK * T * HD * 2)
 
 
+def timed_pdl(fn, args, impl):
+    """timed(), with this library's launches made with programmatic dependent launch when --pdl 1 (ours only)."""
+    if impl != "ours":
+        return timed(fn, args.reps, args.warmup)
+    prev = ops.set_pdl(bool(args.pdl))
+    try:
+        return timed(fn, args.reps, args.warmup)
+    finally:
+        ops.set_pdl(prev)
+
+
 def case_small(args, impl, nseq, seq, nq, nk, hd, rope=False):
     rows, W = nseq * seq, (nq + 2 * nk) * hd
     layers = max(args.layers, 8)  # rotate inputs so consecutive calls do not hit L2
@@ -240,8 +252,8 @@ def case_small(args, impl, nseq, seq, nq, nk, hd, rope=False):
         if rope:  # the reference's two launches; q and k are rotated again on each call (timing only)
             K.rope(qkv[i % layers], cs, sn, None, rows, seq, nq, nk, hd)
         K.attn_full(qkv[i % layers], out, rows, seq, 0, nq, nk, hd, hd ** -0.5)
-    ms = timed(fn, args.reps, args.warmup)
-    return dict(ms=ms, bytes=nbytes, GBps=nbytes / ms / 1e6)
+    ms = timed_pdl(fn, args, impl)
+    return dict(ms=ms, bytes=nbytes, GBps=nbytes / ms / 1e6, pdl=args.pdl if impl == "ours" else 0)
 
 
 def main():
@@ -252,7 +264,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--eager", action="store_true", help="time calls one by one instead of graph replay")
-    ap.add_argument("--pdl", type=int, default=1, help="step case: programmatic dependent launch on/off")
+    ap.add_argument("--pdl", type=int, default=1,
+                    help="programmatic dependent launch on/off for this library's kernels (step, prefill and "
+                         "short-sequence cases)")
     ap.add_argument("--T", type=int, default=1024, help="prefill case: prompt length")
     ap.add_argument("--profile", action="store_true",
                     help="bracket the timed graph replay with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
