@@ -13,8 +13,8 @@
 //               max; the two half-row maxima meet in shared memory at a per-tile barrier of the two warpgroups
 //               (which also votes on whether every wait succeeded, so the loop is left uniformly). It then
 //               exponentiates its 64 columns, keeps its half of the row sum and writes its half of P_j into TMEM
-//               as two bf16 matrices hi + lo (so the weights keep ~16 mantissa bits; O += P_hi.V + P_lo.V), in one
-//               of two P buffers: P_{j+1} is written while P_j.V runs, and a buffer is reused once the P.V two
+//               as two bf16 matrices hi + lo (hi truncated, lo the rounded remainder: ~16 mantissa bits;
+//               O += P_hi.V + P_lo.V), in one of two P buffers: P_{j+1} is written while P_j.V runs, and a buffer is reused once the P.V two
 //               tiles back has read it. It rescales its half of the O row in TMEM when the max has grown by more
 //               than 2^8 (lazy rescaling: until then the stale max is kept, which changes no result because O and
 //               the sum use the same one). The halves of the sum meet once, at the end, and each warpgroup writes
@@ -349,15 +349,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
             }
             if (!ok) continue;
-            // this half of P row r (keys cb .. cb + 63) -> TMEM buffer j & 1 as bf16 pairs: hi (the bf16 of p) in
+            // this half of P row r (keys cb .. cb + 63) -> TMEM buffer j & 1 as bf16 pairs: hi (p truncated) in
             // columns [32wg, 32wg + 32), lo (the rest) in [64 + 32wg, ...); sr[k] takes the k-th hi pair in place
             uint32_t lw[32];
 #pragma unroll
             for (int k = 0; k < 32; k++) {
-                const float p0 = __uint_as_float(sr[2 * k]), p1 = __uint_as_float(sr[2 * k + 1]);
-                const uint32_t hw = pack_bf16x2(p0, p1);
-                const float2 hv = unpack_bf16x2(hw);
-                lw[k] = pack_bf16x2(p0 - hv.x, p1 - hv.y);
+                // hi: p truncated to bf16 (its upper 16 bits, taken with a byte permute instead of a conversion);
+                // lo: the exact remainder p - hi rounded to bf16. hi + lo keeps ~16 bits of p.
+                const uint32_t u0 = sr[2 * k], u1 = sr[2 * k + 1];
+                const float p0 = __uint_as_float(u0), p1 = __uint_as_float(u1);
+                const uint32_t hw = __byte_perm(u0, u1, 0x7632);
+                lw[k] = pack_bf16x2(p0 - __uint_as_float(u0 & 0xffff0000u), p1 - __uint_as_float(u1 & 0xffff0000u));
                 sr[k] = hw;
             }
             const uint32_t tPb = tmem + lane_off + C::P_COL + (j & 1) * 128;
