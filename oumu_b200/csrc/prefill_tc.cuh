@@ -17,8 +17,8 @@
 //               O += P_hi.V + P_lo.V), in one of two P buffers: P_{j+1} is written while P_j.V runs, and a buffer
 //               is reused once the P.V two tiles back has read it. It rescales its half of the O row in TMEM when
 //               the max has grown by more than 2^8 (lazy rescaling: until then the stale max is kept, which changes
-//               no result because O and the sum use the same one). The halves of the sum meet once, at the end, and each warpgroup writes
-//               bf16(O * (1 / sum)) for its 64 columns.
+//               no result because O and the sum use the same one). The halves of the sum meet once, at the end,
+//               and each warpgroup writes bf16(O * (1 / sum)) for its 64 columns.
 // KV epilogue (oumu_attn_prefill_kv, slots > 0): the prompt's k and v also go into every take's cache slot, with TMA
 // tensor stores from the 128-byte-swizzled tiles in shared memory through a map whose extent is the prompt length (rows
 // past it are never written). The CTA of query tile qt copies key tile ntiles - 1 - qt, the G q heads of a kv head
