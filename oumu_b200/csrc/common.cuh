@@ -216,6 +216,8 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap *m, uint32_t src,
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until this thread's committed bulk copies have finished reading their shared-memory sources.
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// ... all but the most recent one
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------------------------------------
 // Warp-level tensor-core fragments (m16n8k16, bf16 in, fp32 accumulate)

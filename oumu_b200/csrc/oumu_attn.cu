@@ -385,6 +385,59 @@ int launch_small_tc(const void *qkv, void *out, int rows, int seq, int causal, i
     return OUMU_OK;
 }
 
+// The plan of the prefill's KV epilogue (pf::CopyPlan). It applies to one causal sequence whose grid plus one copy
+// CTA per q head fits on the SMs at once; it is the same for every q head. A q head's slots are cut into at most
+// PLAN_GROUPS groups. Each key tile t hands its groups, kPfLoopBytes of stores at a time, to the query tiles that
+// load tile t for their attention and not as their last tile (qt > t), shortest first, but never to the two longest
+// query tiles, which bound the kernel: those stores run while the CTA computes. The groups left go one by one to
+// whichever CTA that does not load the tile is expected to be free first: query tile qt is busy until ~kPfFixedUs + (qt + 1) * kPfTileUs, the copy CTA from kPfCopyStartUs, and each
+// group costs its stores at kPfStoreGBs per SM, plus a load of the tile for the first group a CTA takes of it.
+constexpr double kPfFixedUs = 5.0, kPfTileUs = 1.6, kPfCopyStartUs = 1.5, kPfLoadUs = 0.5;
+constexpr double kPfStoreGBs = 85.0, kPfLoopBytes = 256.0 * 1024;
+
+pf::CopyPlan prefill_copy_plan(int hd, int seq, int causal, int nq, int nk, int nseq, int slots, int sms) {
+    pf::CopyPlan plan;
+    std::memset(&plan, 0, sizeof(plan));
+    const int qtiles = (seq + pf::BM - 1) / pf::BM, G = nq / nk;
+    if (slots <= 0 || !causal || nseq != 1 || qtiles > pf::PLAN_MAX || qtiles < 2 ||
+        static_cast<long>(nq) * (qtiles + 1) > sms)
+        return plan;
+    const int per = (slots + G - 1) / G;  // slots per q head (the widest share)
+    int ngroups = std::min(per, pf::PLAN_GROUPS);
+    plan.gs = (per + ngroups - 1) / ngroups;
+    ngroups = (per + plan.gs - 1) / plan.gs;
+    plan.planned = 1;
+    for (int t = 0; t < pf::PLAN_MAX; t++)
+        for (int sg = 0; sg < pf::PLAN_GROUPS; sg++) plan.owner[t][sg] = -1;
+    const double item_bytes = static_cast<double>(plan.gs) * 2 * pf::BN * hd * 2;
+    const double item_us = item_bytes / (kPfStoreGBs * 1e3);
+    const int loop_cap = std::max(1, static_cast<int>(kPfLoopBytes / item_bytes));
+    double busy[pf::PLAN_MAX + 1];
+    for (int q = 0; q < qtiles; q++) busy[q] = kPfFixedUs + (q + 1) * kPfTileUs;
+    busy[qtiles] = kPfCopyStartUs;
+    for (int t = 0; t < qtiles; t++) {
+        int sg = 0;
+        for (int q = t + 1; q < qtiles - 2 && sg < ngroups; q++)
+            for (int k = 0; k < loop_cap && sg < ngroups; k++) plan.owner[t][sg++] = static_cast<signed char>(q);
+        bool loaded[pf::PLAN_MAX + 1] = {};
+        for (; sg < ngroups; sg++) {
+            int best = qtiles;
+            double bt = busy[qtiles] + (loaded[qtiles] ? 0.0 : kPfLoadUs);
+            for (int q = 0; q < t; q++) {
+                const double c = busy[q] + (loaded[q] ? 0.0 : kPfLoadUs);
+                if (c < bt) {
+                    bt = c;
+                    best = q;
+                }
+            }
+            plan.owner[t][sg] = static_cast<signed char>(best);
+            busy[best] = bt + item_us;
+            loaded[best] = true;
+        }
+    }
+    return plan;
+}
+
 // Prefill attention; with kc/vc (slots > 0) also the KV epilogue into every slot's first `seq` positions.
 template <int HD>
 int launch_prefill(const void *qkv, void *out, int rows, int seq, int causal, int nq, int nk, float scale,
@@ -403,9 +456,14 @@ int launch_prefill(const void *qkv, void *out, int rows, int seq, int causal, in
     }
     const int nseq = rows / seq, qtiles = (seq + pf::BM - 1) / pf::BM;
     if (nseq > 65535 || qtiles > 65535) return OUMU_ERR_UNSUPPORTED;
-    dim3 grid(nq, qtiles, nseq);
+    int sms = 0;
+    int rc2 = current_device(&sms);
+    if (rc2) return rc2;
+    const pf::CopyPlan plan = prefill_copy_plan(HD, seq, causal, nq, nk, nseq, slots, sms);
+    dim3 grid(nq, qtiles + (plan.planned ? 1 : 0), nseq);
     OUMU_CK(launch_k(pf::k_attn_prefill<HD>, grid, dim3(pf::NTHREADS), pf::Cfg<HD>::SMEM, st, tm,
-                     static_cast<bf16 *>(out), seq, causal, nq, nk, scale * 1.4426950408889634f, tkc, tvc, slots));
+                     static_cast<bf16 *>(out), seq, causal, nq, nk, scale * 1.4426950408889634f, tkc, tvc, slots,
+                     plan));
     return OUMU_OK;
 }
 

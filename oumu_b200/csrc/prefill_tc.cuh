@@ -54,13 +54,27 @@ struct Cfg {
 // barrier slots (8 bytes each) inside the barrier area
 enum { B_Q = 0, B_KF0 = 1, B_KF1 = 2, B_KE0 = 3, B_KE1 = 4, B_SFULL = 5, B_SFREE = 6, B_PFULL = 7, B_ODONE = 8,
        B_COPY = 9, B_PDONE0 = 10, B_PDONE1 = 11, B_TMEM = 12, B_ABORT = 13, B_VF0 = 14, B_VF1 = 15, B_VE0 = 16,
-       B_VE1 = 17 };
+       B_VE1 = 17, B_COPY1 = 18 };
+
+// Planned KV epilogue: who copies which part of the prompt's k and v into the slots. Without a plan (planned = 0)
+// the CTA of query tile qt copies key tile ntiles - 1 - qt into its q head's share of the slots. With one, the grid
+// has one more row (blockIdx.y = 0) of copy CTAs that only copy, a q head's share of the slots is cut into groups of
+// gs slots, and group sg of key tile t goes to query tile owner[t][sg] or to the copy CTA (owner = the number of
+// query tiles). A CTA copies the groups of the key tiles it loads for its attention as soon as they land (the host
+// gives it at most a few per tile, so the stores have read the stage by the time it is reloaded), and loads the
+// other key tiles it owns groups of after its attention. The host plans so that the long causal query tiles, which
+// bound the kernel, copy little, and no SM stores more than its share: one SM writes ~85 GB/s with TMA stores.
+constexpr int PLAN_MAX = 32, PLAN_GROUPS = 8;
+struct CopyPlan {
+    int planned, gs;
+    signed char owner[PLAN_MAX][PLAN_GROUPS];
+};
 
 template <int HD>
 __global__ void __launch_bounds__(NTHREADS, 1)
     k_attn_prefill(const __grid_constant__ CUtensorMap tqkv, bf16 *__restrict__ out, int seq, int causal, int nq,
                    int nk, float sl2, const __grid_constant__ CUtensorMap tkc,
-                   const __grid_constant__ CUtensorMap tvc, int slots) {
+                   const __grid_constant__ CUtensorMap tvc, int slots, const __grid_constant__ CopyPlan plan) {
     using C = Cfg<HD>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_s = smem_u32(smem_raw);
@@ -73,7 +87,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // CTAs start in block order, x fastest: every head's heaviest causal tile first, then the next heaviest, ... so
-    // that the tiles left for the last wave are the short ones
+    // that the tiles left for the last wave are the short ones. A planned KV epilogue puts the copy CTAs first
+    // (blockIdx.y = 0, qt = the number of query tiles).
+    const bool planned = slots > 0 && plan.planned != 0;
+    const bool copier = planned && blockIdx.y == 0;
     const int qt = gridDim.y - 1 - blockIdx.y;
     const int h = blockIdx.x, n = blockIdx.z, G = nq / nk, kh = h / G;
     const int q0 = qt * BM;
@@ -96,6 +113,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         mbar_init(bar(B_PFULL), 8);
         mbar_init(bar(B_ODONE), 1);
         mbar_init(bar(B_COPY), 1);
+        mbar_init(bar(B_COPY1), 1);
         mbar_init(bar(B_PDONE0), 1);
         mbar_init(bar(B_PDONE1), 1);
         *abort_flag = 0;
@@ -104,7 +122,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // Programmatic dependent launch: the set-up above overlaps the preceding kernel; TMEM is allocated only after it
     // has completed (a kernel that takes all 512 columns before its predecessor ends could hold columns that
     // predecessor has yet to allocate), and the next kernel is let in only once the columns are held.
-    if (warp == 1) {
+    if (warp == 1 && !copier) {
         pdl_wait();
         tmem_alloc(bar(B_TMEM), C::TMEM_COLS);
         tmem_relinquish();
@@ -119,17 +137,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // ------------------------------ TMA producer ------------------------------
         // Lane 0 issues the loads; the KV epilogue's stores are spread over the warp's 32 lanes (one thread keeps
         // only a few bulk copies in flight). Every wait is taken by the whole warp, so control flow stays uniform.
+        if (copier) pdl_wait();  // the copy CTAs allocate no TMEM, so no other thread of theirs has waited
         if (lane == 0) {
             tma_prefetch_desc(&tqkv);
-            mbar_expect_tx(bar(B_Q), C::NBOX * BOX);
+            if (!copier) {
+                mbar_expect_tx(bar(B_Q), C::NBOX * BOX);
 #pragma unroll
-            for (int bx = 0; bx < C::NBOX; bx++)
-                tma_load_2d(sm_s + C::Q_OFF + bx * BOX, &tqkv, bar(B_Q), h * HD + bx * 64, row0 + q0);
+                for (int bx = 0; bx < C::NBOX; bx++)
+                    tma_load_2d(sm_s + C::Q_OFF + bx * BOX, &tqkv, bar(B_Q), h * HD + bx * 64, row0 + q0);
+            }
         }
-        // this CTA's share of the KV epilogue: key tile cj of kv head kh into slots [s0, s1)
+        // this CTA's share of the KV epilogue: key tile cj (or the plan's tiles) of kv head kh into slots [s0, s1)
         const int cj = ntiles_all - 1 - qt, g = h % G;
         const int per = slots > 0 ? (slots + G - 1) / G : 0, s0 = g * per, s1 = min(slots, s0 + per);
-        const bool copy = slots > 0 && causal && s0 < s1;
+        const bool copy = !planned && slots > 0 && causal && s0 < s1;
         // K (v = 0) or V (v = 1) of key tile tj into stage stg, completing its bytes on barrier fb. tx > 0: this call
         // is the barrier's one arrival, expecting tx bytes; tx == 0: the bytes count against an earlier expectation.
         auto load_half = [&](int v, int stg, int tj, uint32_t fb, uint32_t tx) {
@@ -142,12 +163,30 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             __syncwarp();
         };
-        auto store_tile = [&](int stg) {  // (slot, box, K or V) items over the lanes
-            const int items = (s1 - s0) * C::NBOX * 2;
+        // slots [a, b) of key tile `tile` from stage stg: (slot, box, K or V) items over the lanes
+        auto store_slots = [&](int stg, int tile, int a, int b) {
+            const int items = (b - a) * C::NBOX * 2;
             for (int it = lane; it < items; it += 32) {
-                const int kv = it & 1, bx = (it >> 1) % C::NBOX, sl = s0 + (it >> 1) / C::NBOX;
+                const int kv = it & 1, bx = (it >> 1) % C::NBOX, sl = a + (it >> 1) / C::NBOX;
                 tma_store_3d(kv ? &tvc : &tkc, sm_s + (kv ? C::V_OFF : C::K_OFF) + (stg * C::NBOX + bx) * BOX,
-                             bx * 64, cj * BN, sl * nk + kh);
+                             bx * 64, tile * BN, sl * nk + kh);
+            }
+        };
+        auto store_tile = [&](int stg, int tile) {
+            store_slots(stg, tile, s0, s1);
+            bulk_commit();
+        };
+        // planned: whether this CTA owns slot groups of key tile t (none past the plan's tiles)
+        auto owns = [&](int t) {
+            if (!planned || t < 0 || t >= PLAN_MAX || s0 >= s1) return false;
+            for (int sg = 0; sg < PLAN_GROUPS; sg++)
+                if (plan.owner[t][sg] == qt) return true;
+            return false;
+        };
+        auto store_owned = [&](int stg, int t) {  // one bulk group per call
+            for (int sg = 0; sg < PLAN_GROUPS; sg++) {
+                const int a = s0 + sg * plan.gs, b = min(s1, a + plan.gs);
+                if (plan.owner[t][sg] == qt && a < b) store_slots(stg, t, a, b);
             }
             bulk_commit();
         };
@@ -156,59 +195,110 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             return __all_sync(0xffffffffu, mbar_wait(bar(B_KF0 + (t & 1)), (t >> 1) & 1) &&
                                                mbar_wait(bar(B_VF0 + (t & 1)), (t >> 1) & 1));
         };
-        // The V loads trail the K loads by one tile (K0, K1, V0, K2, V1, ...): K_j waits only for S_{j-2}, never
-        // behind the wait of a V stage for its P.V.
+        // planned epilogue, the key tiles from t0 on that this CTA owns groups of: loaded in turn into stages 0 and 1
+        // (free: a copy CTA has no attention, and the others come here after the last use of both stages) and stored
+        // from there; a stage is reloaded only once the stores of the tile two back have read it
+        auto copy_planned = [&](int t0) {
+            bool good = true;
+            int i = 0;
+            bulk_wait_read();  // the stores made during the attention have read their stages
+            __syncwarp();
+            for (int t = t0; t < ntiles_all && good; t++) {
+                if (!owns(t)) continue;
+                const int st = i & 1;
+                const uint32_t cb = bar(st ? B_COPY1 : B_COPY);
+                if (i >= 2) {  // every lane's stores of the tile two back have read the stage before lane 0 reloads it
+                    bulk_wait_read_1();
+                    __syncwarp();
+                }
+                load_half(0, st, t, cb, 2 * C::NBOX * BOX);
+                load_half(1, st, t, cb, 0);
+                good = __all_sync(0xffffffffu, *abort_flag == 0 && mbar_wait(cb, (i >> 1) & 1));
+                if (good) store_owned(st, t);
+                i++;
+            }
+            bulk_wait_read();  // shared memory stays in place until every store has read it
+            return good;
+        };
         bool ok = true, stored = false;
-        for (int j = 0; j <= ntiles; j++) {
-            if (j < ntiles) {
-                const int st = j & 1;
-                if (j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KE0 + st), ((j >> 1) - 1) & 1));
-                ok = __all_sync(0xffffffffu, ok && *abort_flag == 0);
-                if (!ok) break;
-                if (copy && stored && j == cj + 2) bulk_wait_read();  // the copy of tile cj has read this stage
-                load_half(0, st, j, bar(B_KF0 + st), C::NBOX * BOX);
-            }
-            if (j >= 1) {
-                const int v = j - 1, sv = v & 1;
-                if (v >= 2) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_VE0 + sv), ((v >> 1) - 1) & 1));
-                if (!ok) break;
-                load_half(1, sv, v, bar(B_VF0 + sv), C::NBOX * BOX);
-                if (copy && v == cj) {  // tile cj goes out as soon as both its halves have landed
-                    ok = landed(cj);
+        if (copier) {
+            ok = copy_planned(0);
+            if (!ok && lane == 0) *abort_flag = 1;
+            __syncwarp();
+        } else {
+            // The V loads trail the K loads by one tile (K0, K1, V0, K2, V1, ...): K_j waits only for S_{j-2}, never
+            // behind the wait of a V stage for its P.V.
+            for (int j = 0; j <= ntiles; j++) {
+                if (j < ntiles) {
+                    const int st = j & 1;
+                    if (j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KE0 + st), ((j >> 1) - 1) & 1));
+                    ok = __all_sync(0xffffffffu, ok && *abort_flag == 0);
                     if (!ok) break;
-                    store_tile(cj & 1);
-                    stored = true;
+                    if ((copy && stored && j == cj + 2) || owns(j - 2)) {
+                        // the stores of tile j - 2 (the latest bulk group) have read this stage, every lane's
+                        bulk_wait_read();
+                        __syncwarp();
+                    }
+                    load_half(0, st, j, bar(B_KF0 + st), C::NBOX * BOX);
                 }
-            }
-        }
-        if (ok && copy && !stored) {
-            if (cj < ntiles) {
-                // the CTA's last tile: still in its stage
-                ok = landed(cj);
-                if (ok) {
-                    store_tile(cj & 1);
-                    stored = true;
-                }
-            } else {
-                // a tile this CTA does not attend to: into stage 0 once its last use there (tile jl) is done
-                const int jl = (ntiles - 1) & ~1;
-                ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KE0), (jl >> 1) & 1) &&
-                                                 mbar_wait(bar(B_VE0), (jl >> 1) & 1));
-                if (ok) {
-                    load_half(0, 0, cj, bar(B_COPY), 2 * C::NBOX * BOX);
-                    load_half(1, 0, cj, bar(B_COPY), 0);
-                    ok = __all_sync(0xffffffffu, mbar_wait(bar(B_COPY), 0));
-                    if (ok) {
-                        store_tile(0);
+                if (j >= 1) {
+                    const int v = j - 1, sv = v & 1;
+                    if (v >= 2) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_VE0 + sv), ((v >> 1) - 1) & 1));
+                    if (!ok) break;
+                    load_half(1, sv, v, bar(B_VF0 + sv), C::NBOX * BOX);
+                    if (copy && v == cj) {  // tile cj goes out as soon as both its halves have landed
+                        ok = landed(cj);
+                        if (!ok) break;
+                        store_tile(cj & 1, cj);
+                        stored = true;
+                    }
+                    if (owns(v)) {  // planned: this CTA's groups of tile v, as soon as it has landed
+                        ok = landed(v);
+                        if (!ok) break;
+                        store_owned(v & 1, v);
                         stored = true;
                     }
                 }
             }
+            if (ok && copy && !stored) {
+                if (cj < ntiles) {
+                    // the CTA's last tile: still in its stage
+                    ok = landed(cj);
+                    if (ok) {
+                        store_tile(cj & 1, cj);
+                        stored = true;
+                    }
+                } else {
+                    // a tile this CTA does not attend to: into stage 0 once its last use there (tile jl) is done
+                    const int jl = (ntiles - 1) & ~1;
+                    ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KE0), (jl >> 1) & 1) &&
+                                                     mbar_wait(bar(B_VE0), (jl >> 1) & 1));
+                    if (ok) {
+                        load_half(0, 0, cj, bar(B_COPY), 2 * C::NBOX * BOX);
+                        load_half(1, 0, cj, bar(B_COPY), 0);
+                        ok = __all_sync(0xffffffffu, mbar_wait(bar(B_COPY), 0));
+                        if (ok) {
+                            store_tile(0, cj);
+                            stored = true;
+                        }
+                    }
+                }
+            }
+            if (ok && planned) {
+                // the last use of each stage (the last tile j of its parity: S read its K, P.V its V) must be done
+                for (int st = 0; st < 2 && ok; st++) {
+                    if (ntiles <= st) continue;
+                    const int jl = ((ntiles - 1 - st) & ~1) + st;
+                    ok = __all_sync(0xffffffffu, mbar_wait(bar(B_KE0 + st), (jl >> 1) & 1) &&
+                                                     mbar_wait(bar(B_VE0 + st), (jl >> 1) & 1));
+                }
+                if (ok) ok = copy_planned(ntiles);
+            }
+            if (stored) bulk_wait_read();  // shared memory stays in place until every store has read it
+            if (!ok && lane == 0) *abort_flag = 1;
+            __syncwarp();  // the warp reaches the final CTA barrier converged
         }
-        if (stored) bulk_wait_read();  // shared memory stays in place until every store has read it
-        if (!ok && lane == 0) *abort_flag = 1;
-        __syncwarp();  // the warp reaches the final CTA barrier converged
-    } else if (warp == 1) {
+    } else if (warp == 1 && !copier) {
         // ------------------------------ MMA issuer ------------------------------
         if (lane == 0) {
             const uint32_t idS = idesc_bf16_f32(BM, BN, 0, 0);
@@ -260,7 +350,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (!ok) *abort_flag = 1;
         }
         __syncwarp();
-    } else {
+    } else if (!copier) {
         // ------------------------------ softmax / correction / epilogue ------------------------------
         const int quarter = warp & 3, wg = (warp - 2) >> 2;
         const int r = quarter * 32 + lane;  // query row within the tile
@@ -370,7 +460,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(B_PFULL));
         }
-        if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE), (ntiles - 1) & 1));
+        // O is final once the last P.V has completed: waited on that P buffer's barrier, whose phase before it (the
+        // P.V two tiles back) this loop has already waited for, so the parity names one phase only. (B_ODONE could
+        // still be two phases behind here, where a parity wait cannot tell the phase awaited from the one before.)
+        if (ok && ntiles > 0)
+            ok = __all_sync(0xffffffffu,
+                            mbar_wait(bar(B_PDONE0 + ((ntiles - 1) & 1)), ((ntiles - 1) >> 1) & 1));
         if (!ok) *abort_flag = 1;
         // the two halves of each row sum meet in shared memory
         float *lx = reinterpret_cast<float *>(sm + C::LX_OFF);
@@ -402,7 +497,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == 1 && !copier) {
         tc_fence_after();
         tmem_dealloc(tmem, C::TMEM_COLS);
     }

@@ -217,10 +217,10 @@ def case_prefill_kv(args, B=64, maxlen=4096, T=1024):
         ops.attn_full(qkv[i % layers], out, T, T, 1, NQ, NK, HD, HD ** -0.5)
         ops.kv_replicate(kc, B, NK, maxlen, HD, T)
         ops.kv_replicate(vc, B, NK, maxlen, HD, T)
-    ms = timed(fused, args.reps, args.warmup)
-    ms_sep = timed(separate, args.reps, args.warmup)
+    ms = timed_pdl(fused, args, "ours")
+    ms_sep = timed_pdl(separate, args, "ours")
     return dict(ms=ms, ms_separate=ms_sep, flops=flops, TFLOPs=flops / ms / 1e9,
-                kv_bytes_written=2 * B * NK * T * HD * 2)
+                kv_bytes_written=2 * B * NK * T * HD * 2, pdl=args.pdl)
 
 
 def timed_pdl(fn, args, impl):

@@ -57,3 +57,26 @@ def test_prefill_kv_rejects_short_prompts(cuda):
     kc = torch.zeros((2, 2, 64, 128), dtype=torch.bfloat16, device="cuda")
     with pytest.raises(_lib.OumuError):
         ops.attn_prefill_kv(qkv, out, kc, kc.clone(), 16, 2, 16, 2, 128, 64, 128 ** -0.5)
+
+
+def test_prefill_kv_config3_repeated(cuda):
+    """Config 3 called twelve times on fresh inputs, each output bit-identical to oumu_attn_full's. The planned
+    epilogue (copy CTAs, stores spread over the query tiles) changes when the V loads land; a wait for the last P.V
+    that could pass on the P.V before it once showed here as a wrong query tile in 2 of 6 calls."""
+    T, slots, nq, nk, hd, maxlen = 1024, 64, 16, 2, 128, 4096
+    scale = hd ** -0.5
+    k = torch.zeros((slots, nk, maxlen, hd), dtype=torch.bfloat16, device="cuda")
+    v = torch.zeros_like(k)
+    for trial in range(12):
+        qkv = rnd((T, (nq + 2 * nk) * hd), 100 + trial)
+        want = torch.empty((T, nq * hd), dtype=torch.bfloat16, device="cuda")
+        ops.attn_full(qkv, want, T, T, 1, nq, nk, hd, scale)
+        got = torch.zeros_like(want)
+        ops.attn_prefill_kv(qkv, got, k, v, T, slots, nq, nk, hd, maxlen, scale)
+        torch.cuda.synchronize()
+        bad = (got != want).view(T // 128, 128, -1).any(dim=2).any(dim=1)
+        assert not bad.any(), f"call {trial}: query tiles {bad.nonzero().flatten().tolist()} differ"
+        kref = qkv[:, nq * hd:(nq + nk) * hd].view(T, nk, hd).permute(1, 0, 2)
+        vref = qkv[:, (nq + nk) * hd:].view(T, nk, hd).permute(1, 0, 2)
+        assert torch.equal(k[:, :, :T], kref.expand(slots, -1, -1, -1)), f"call {trial}: k slots"
+        assert torch.equal(v[:, :, :T], vref.expand(slots, -1, -1, -1)), f"call {trial}: v slots"
