@@ -58,8 +58,9 @@ cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
 
 constexpr int kMaxDevices = 64;
 // Weight-streaming GEMM: pipeline depth per token tile (shared memory: stages x (16 KB + tile x 128 B) + the
-// inbox).
-constexpr int kGemmStages32 = 4, kGemmStages64 = 4, kGemmStages128 = 3;
+// inbox). At 32 tokens, 8 stages keep 160 KB of weights in flight per SM: a GEMM whose tiles occupy only part of the
+// SMs (gate|up on 96) still streams at the HBM rate (captured decoding step: 4.69 -> 4.55 ms against 4 stages).
+constexpr int kGemmStages32 = 8, kGemmStages64 = 4, kGemmStages128 = 3;
 
 constexpr int kSmemMax = 227 * 1024;
 
