@@ -45,6 +45,10 @@ constexpr int GMAX = 8;      // q heads per kv head handled by one mma column bl
 constexpr int STAGES = 2 * NCW;
 constexpr int NFB = 1;       // flush buffer between the consumers and the merger
 constexpr int MIN_TILES = 4; // tiles per CTA at least: small problems use fewer CTAs rather than many 1-tile partials
+// ... and no segment split over more than about MAX_SPLIT CTAs, with ranges of up to SPLIT_TILES_MAX tiles: a split
+// segment's last contributor merges every partial in turn, so one long take decoded alone is better served by a few
+// CTAs with more tiles each (one take of 4096 positions: 23.7 -> 14.7 us; of 16384: 44.3 -> 31.4 us)
+constexpr int MAX_SPLIT = 8, SPLIT_TILES_MAX = 64;
 
 template <int HD>
 struct Cfg {
@@ -403,7 +407,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t bar_fempty = bar_ffull + 8 * NFB;    // flush buffer b merged, free again
     int *pre = reinterpret_cast<int *>(sm + L.pre_off());
     int *Ls = reinterpret_cast<int *>(sm + L.len_off());
-    volatile int *misc = reinterpret_cast<volatile int *>(sm + L.misc_off());  // [abort, bcast consumers, bcast merger]
+    volatile int *misc = reinterpret_cast<volatile int *>(sm + L.misc_off());  // [abort, bcast, bcast, longest]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int B = P.B, nk = P.nk, G = P.nq / P.nk;
@@ -411,7 +415,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // ---- per-take lengths and the tile prefix over takes (warp 0) ----
     if (warp == 0) {
         const int per = (B + 31) / 32, s0 = lane * per;
-        int sum = 0;
+        int sum = 0, tmax = 0;
         for (int k = 0; k < per; k++) {
             int s = s0 + k;
             if (s < B) {
@@ -421,9 +425,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     Lv = Lv < 1 ? 1 : P.maxlen;
                 }
                 Ls[s] = Lv;
-                sum += ((Lv + TILE - 1) / TILE) * nk;
+                const int T = (Lv + TILE - 1) / TILE;
+                sum += T * nk;
+                tmax = T > tmax ? T : tmax;
             }
         }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) tmax = max(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+        if (lane == 0) misc[3] = tmax;  // the longest segment, in tiles
         int incl = sum;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -454,9 +463,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __syncthreads();
 
     // Effective grid: at most one CTA per MIN_TILES tiles, so every CTA range [c*W/Gc, (c+1)*W/Gc) is non-empty and
-    // every CTA between the first and the last of a segment contributes a partial to it.
+    // every CTA between the first and the last of a segment contributes a partial to it; and fewer, longer ranges when
+    // the longest segment would otherwise be split over more than about MAX_SPLIT CTAs.
     const long W = pre[B];
-    const long want = (W + MIN_TILES - 1) / MIN_TILES;
+    const int split_tiles = min((misc[3] + MAX_SPLIT - 1) / MAX_SPLIT, SPLIT_TILES_MAX);
+    const long min_tiles = split_tiles > MIN_TILES ? split_tiles : MIN_TILES;
+    const long want = (W + min_tiles - 1) / min_tiles;
     const int Gc = static_cast<int>(want < static_cast<long>(gridDim.x) ? want : static_cast<long>(gridDim.x));
     const int c = blockIdx.x;
     if (threadIdx.x == 0) pdl_trigger();

@@ -374,3 +374,13 @@ def test_device_error_word(cuda):
     assert bool(torch.isfinite(att.float()).all())
     assert ops.device_error(reset=True) & 2
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("L", [4096, 16384])
+def test_decode_one_long_take(cuda, L):
+    # one take decoded alone over a long context: the grid shrinks so that each segment is split over at most ~8
+    # CTAs (16 CTAs of 16 tiles at 4096 positions, 64 CTAs of 64 tiles at 16384)
+    B, maxlen = 1, L
+    qkv, kc, vc, ln = decode_case(B, [L], maxlen, seed=41)
+    att, _ = run_decode(qkv, kc, vc, ln, B, maxlen)
+    gc.assert_close(u16(att), oracle_decode(qkv, kc, vc, [L], B, maxlen), f"one take, L={L}")
