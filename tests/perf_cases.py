@@ -7,6 +7,7 @@ Also the small, self-contained cases used for ncu captures.
 CASE: decode (config 2: 64 takes, slots of 4096, lengths U[330,4096]; per layer)
       step (config 2 per layer: decode prologue + attention)
       decode1 (config 1: one take, 512 of 4096 positions)
+      decode1_long (one take, all 4096 positions of its slot)
       prefill (config 3: T = 1024 causal, 16 q / 2 kv heads, hd 128; per layer; --T for other prompt lengths)
       replicate (config 3: the prompt KV of one layer, K and V, into 64 slots of 4096)
       prefill_kv (config 3 per layer in one launch: prefill + k/v into all 64 slots; and the separate launches)
@@ -287,6 +288,8 @@ def main():
         r = case_decode(args, args.impl, lens2, shared=True)
     elif c == "decode1":
         r = case_decode(args, args.impl, [512])
+    elif c == "decode1_long":
+        r = case_decode(args, args.impl, [4096])
     elif c == "prefill":
         r = case_prefill(args, args.impl, T=args.T)
     elif c == "replicate":
