@@ -80,3 +80,36 @@ def test_prefill_kv_config3_repeated(cuda):
         vref = qkv[:, (nq + nk) * hd:].view(T, nk, hd).permute(1, 0, 2)
         assert torch.equal(k[:, :, :T], kref.expand(slots, -1, -1, -1)), f"call {trial}: k slots"
         assert torch.equal(v[:, :, :T], vref.expand(slots, -1, -1, -1)), f"call {trial}: v slots"
+
+
+def _sweep_cases(n=16, seed=5):
+    import random
+    rng = random.Random(seed)
+    out = []
+    for _ in range(n):
+        nq, nk = rng.choice([(16, 2), (8, 8), (32, 4), (16, 16), (8, 1), (24, 3)])
+        T = rng.choice([17, 100, 129, 200, 255, 384, 511, 640, 900, 1024, 1100, 1500])
+        out.append((T, rng.choice([1, 2, 3, 5, 9, 17, 33, 64, 96]), nq, nk, rng.choice([64, 128]),
+                    T + rng.choice([0, 1, 7, 64, 300])))
+    return out
+
+
+@pytest.mark.parametrize("T,slots,nq,nk,hd,maxlen", _sweep_cases())
+def test_prefill_kv_random_shapes(cuda, T, slots, nq, nk, hd, maxlen):
+    """Seeded random shapes through both KV epilogues (the planned one where the grid and its copy CTAs fit on the
+    SMs at once, the mirror scheme elsewhere): bit-identical to attn_full + kv_write + kv_replicate."""
+    W = (nq + 2 * nk) * hd
+    scale = hd ** -0.5
+    qkv = rnd((T, W), T + slots)
+    want = torch.empty((T, nq * hd), dtype=torch.bfloat16, device="cuda")
+    ops.attn_full(qkv, want, T, T, 1, nq, nk, hd, scale)
+    k0, v0 = rnd((slots, nk, maxlen, hd), 7), rnd((slots, nk, maxlen, hd), 8)
+    wk, wv = k0.clone(), v0.clone()
+    ops.kv_write(qkv, wk, wv, None, 1, T, nq, nk, hd, maxlen)
+    ops.kv_replicate(wk, slots, nk, maxlen, hd, T)
+    ops.kv_replicate(wv, slots, nk, maxlen, hd, T)
+    got, gk, gv = torch.zeros_like(want), k0.clone(), v0.clone()
+    ops.attn_prefill_kv(qkv, got, gk, gv, T, slots, nq, nk, hd, maxlen, scale)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want), "attention output"
+    assert torch.equal(gk, wk) and torch.equal(gv, wv), "slots"
