@@ -61,9 +61,10 @@ enum { B_Q = 0, B_KF0 = 1, B_KF1 = 2, B_KE0 = 3, B_KE1 = 4, B_SFULL = 5, B_SFREE
 // has one more row (blockIdx.y = 0) of copy CTAs that only copy, a q head's share of the slots is cut into groups of
 // gs slots, and group sg of key tile t goes to query tile owner[t][sg] or to the copy CTA (owner = the number of
 // query tiles). A CTA copies the groups of the key tiles it loads for its attention as soon as they land (the host
-// gives it at most a few per tile, so the stores have read the stage by the time it is reloaded), and loads the
-// other key tiles it owns groups of after its attention. The host plans so that the long causal query tiles, which
-// bound the kernel, copy little, and no SM stores more than its share: one SM writes ~85 GB/s with TMA stores.
+// gives it at most a few per tile, so the wait for those stores to have read the stage before it is reloaded is
+// short), and loads the other key tiles it owns groups of after its attention. The host plans so that the longest
+// causal query tiles, which bound the kernel, copy nothing while they compute, and no SM stores much more than its
+// share: one SM writes only ~85 GB/s with TMA stores.
 constexpr int PLAN_MAX = 32, PLAN_GROUPS = 8;
 struct CopyPlan {
     int planned, gs;
