@@ -409,16 +409,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 m = mt;
             }
             const float mref = m == -INFINITY ? 0.f : m;
-            float rs8[8];
+            // p = 2^(s * sl2 - mref) per column, summed in eight independent chains (column c into chain c % 8),
+            // the scaling and the sums two columns per packed instruction
+            float2 rs2[4];
 #pragma unroll
-            for (int k = 0; k < 8; k++) rs8[k] = 0.f;
+            for (int k = 0; k < 4; k++) rs2[k] = make_float2(0.f, 0.f);
+            const float2 sl2v = make_float2(sl2, sl2), nmref = make_float2(-mref, -mref);
 #pragma unroll
-            for (int c = 0; c < 64; c++) {  // eight independent sum chains
-                const float p = fast_exp2(fmaf(__uint_as_float(sr[c]), sl2, -mref));
-                rs8[c & 7] += p;
-                sr[c] = __float_as_uint(p);
+            for (int i = 0; i < 32; i++) {
+                const float2 x = fma2(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sl2v,
+                                      nmref);
+                const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+                rs2[i & 3] = add2(rs2[i & 3], p);
+                sr[2 * i] = __float_as_uint(p.x);
+                sr[2 * i + 1] = __float_as_uint(p.y);
             }
-            const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+            const float rs = ((rs2[0].x + rs2[0].y) + (rs2[1].x + rs2[1].y)) +
+                             ((rs2[2].x + rs2[2].y) + (rs2[3].x + rs2[3].y));
             l = l * alpha + rs;
             // P_j goes into buffer j & 1 once PV_{j-2} has read it; O may be rescaled once PV_{j-1} has completed.
             // A wait that times out here ends the loop at the next tile's vote.
@@ -448,9 +455,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 // hi: p truncated to bf16 (its upper 16 bits, taken with a byte permute instead of a conversion);
                 // lo: the exact remainder p - hi rounded to bf16. hi + lo keeps ~16 bits of p.
                 const uint32_t u0 = sr[2 * k], u1 = sr[2 * k + 1];
-                const float p0 = __uint_as_float(u0), p1 = __uint_as_float(u1);
                 const uint32_t hw = __byte_perm(u0, u1, 0x7632);
-                lw[k] = pack_bf16x2(p0 - __uint_as_float(u0 & 0xffff0000u), p1 - __uint_as_float(u1 & 0xffff0000u));
+                const float2 lo = sub2(make_float2(__uint_as_float(u0), __uint_as_float(u1)),
+                                       make_float2(__uint_as_float(u0 & 0xffff0000u), __uint_as_float(u1 & 0xffff0000u)));
+                lw[k] = pack_bf16x2(lo.x, lo.y);
                 sr[k] = hw;
             }
             const uint32_t tPb = tmem + lane_off + C::P_COL + (j & 1) * 128;
