@@ -466,19 +466,25 @@ def main():
     #      LAYERS launches of the fused decode layer per step, CUDA events on the launching stream) ----
     launch_ms = ms / (args.steps * LAYERS)
     achieved = per_layer / (launch_ms / 1e3) / 1e9
-    # and the same kernel launched alone, eagerly (no neighbour to overlap its ramp-up and tail), for reference
+    # and the same launches serialised, for reference: the step captured without programmatic dependent launch, so
+    # each launch starts only once the one before it has completed and its ramp-up and tail overlap nothing. (Events
+    # around eager launches would add the host's launch time whenever it exceeds a kernel's.)
+    graph_ser = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph_ser, stream=stream):
+            step()
+    torch.cuda.current_stream().wait_stream(stream)
     reps = max(2, min(10, args.steps // 20))
-    durs = []
-    for _ in range(reps):
-        for l in range(LAYERS):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            ops.attn_decode(qkv_all[l], kc[l], vc[l], att_all[l], ws, None, ln, TAKES, NQ, NK, HD, MAXLEN,
-                            HD ** -0.5)
-            b.record()
-            durs.append((a, b))
+    graph_ser.replay()
     torch.cuda.synchronize()
-    kern_ms_local = statistics.mean(a.elapsed_time(b) for a, b in durs)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        graph_ser.replay()
+    b.record()
+    torch.cuda.synchronize()
+    del graph_ser
+    kern_ms_local = a.elapsed_time(b) / (reps * LAYERS)
     kern_ms = max_over_ranks(kern_ms_local)
     peak, peak_kind = measured_peak()
     traffic = committed_traffic()
