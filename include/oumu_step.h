@@ -96,6 +96,19 @@ int oumu_decode_loop_destroy(oumu_decode_loop_t loop);
 int oumu_gemm(const void *x, int ldx, const void *w, void *y, int ldy, const void *bias, int M, int N, int K,
               oumu_stream_t stream);
 
+/*
+ * The SwiGLU MLP's input projection and activation in one launch: act[m][i] (row pitch ldact >= F) =
+ * bf16(bf16(silu(g)) * u) for i < F, with g = bf16(x[m] . Wg[i] (+ bg[i])) and u = bf16(x[m] . Wu[i] (+ bu[i])), the
+ * values oumu_gemm would store for the gate | up projection and the arithmetic of silu_mul (kernels/voxcpm.cu:92-99):
+ * the output is bit-identical to oumu_gemm into [M][2F] followed by oumu_silu_mul, without the [M][2F] intermediate
+ * or the second launch (Engine's Mlp: the gate|up Lin, then silu_mul, src/model.rs:627-628). w_il is the gate|up
+ * weight [2F][K] with its rows interleaved in groups of 8: rows [16j, 16j + 8) are gate rows [8j, 8j + 8) and rows
+ * [16j + 8, 16j + 16) are up rows [8j, 8j + 8) (bias_il, if not NULL, interleaved the same way); a host permutes the
+ * weight once when it loads it. F a multiple of 8; the other requirements are oumu_gemm's with N = 2F.
+ */
+int oumu_gemm_swiglu(const void *x, int ldx, const void *w_il, void *act, int ldact, const void *bias_il, int M,
+                     int F, int K, oumu_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -44,6 +44,7 @@ SIGNATURES = {
     "oumu_cfg_euler": (_I, [_P, _P, _I, _I, _I, _F, _F, _P]),
     "oumu_step_end": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "oumu_gemm": (_I, [_P, _I, _P, _P, _I, _P, _I, _I, _I, _P]),
+    "oumu_gemm_swiglu": (_I, [_P, _I, _P, _P, _I, _P, _I, _I, _I, _P]),
     "oumu_decode_loop_create": (_I, [_P, _P, _P, _P, _I, _I, ctypes.POINTER(_P)]),
     "oumu_decode_loop_launch": (_I, [_P, _P]),
     "oumu_decode_loop_destroy": (_I, [_P]),

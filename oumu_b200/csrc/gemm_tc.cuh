@@ -17,6 +17,11 @@
 //     not depend on the preceding kernel, so their loads overlap its tail), warp 1 owns TMEM and issues
 //     tcgen05.mma, warps 2-5 move the accumulator from TMEM to the owners' inboxes (thread = weight row); all six
 //     warps reduce.
+// SwiGLU form (Params::act): W holds the gate and up rows of an MLP interleaved in groups of 8 (rows [16j, 16j + 8)
+// are gate rows [8j, 8j + 8), rows [16j + 8, 16j + 16) the up rows of the same indices), so each owner's row range
+// (whole groups of 16) holds both halves of its outputs; the reduction rounds gate and up to bf16 as the plain form
+// would store them and writes act[m][8j + i] = bf16(bf16(silu(gate)) * up), the arithmetic of the separate
+// silu_mul kernel (kernels/voxcpm.cu:92-99), so the result is bit-identical to the GEMM followed by silu_mul.
 // All mbarrier waits are bounded (mbar_wait); on a timeout the kernel records the error and still reaches the
 // cluster barrier (its output is then garbage, and the error word says so).
 #pragma once
@@ -30,9 +35,10 @@ constexpr int NTHREADS = 6 * 32;      // TMA, MMA, 4 epilogue warps
 constexpr int W_BYTES = BW * BK * 2;  // 16 KB
 constexpr int MAX_SPLIT = 8;          // portable cluster size
 
-// Rows of a tile each CTA of a split-C cluster owns (whole groups of 8).
-__host__ __device__ constexpr int rows_per_owner(int split) {
-    return ((BW / split + (BW % split ? 1 : 0) + 7) / 8) * 8;
+// Rows of a tile each CTA of a split-C cluster owns: whole groups of 8, or of 16 in the SwiGLU form (a gate group
+// and its up group).
+__host__ __device__ constexpr int rows_per_owner(int split, int act = 0) {
+    return ((BW / split + (BW % split ? 1 : 0) + (act ? 15 : 7)) / (act ? 16 : 8)) * (act ? 16 : 8);
 }
 
 template <int TN, int STAGES>
@@ -45,8 +51,10 @@ struct Cfg {
     static constexpr int INBOX_OFF = STAGE_OFF + STAGES * STAGE_BYTES;
     static constexpr uint32_t TMEM_COLS = TN;              // 32, 64 or 128: a power of two >= 32
     // inbox: the split partials of the owned rows, [split][rows_per_owner][TN] fp32
-    static constexpr int inbox_bytes(int split) { return split * rows_per_owner(split) * TN * 4; }
-    static constexpr int smem_bytes(int split) { return INBOX_OFF + inbox_bytes(split) + 1024; }  // + alignment
+    static constexpr int inbox_bytes(int split, int act = 0) { return split * rows_per_owner(split, act) * TN * 4; }
+    static constexpr int smem_bytes(int split, int act = 0) {  // + alignment
+        return INBOX_OFF + inbox_bytes(split, act) + 1024;
+    }
 };
 
 struct Params {
@@ -55,7 +63,47 @@ struct Params {
     int ldy, M, N;
     int NT, KB;  // weight tiles, K blocks of 64
     int split;   // CTAs per tile = the cluster size
+    int act;     // 0: y = x.W^T (+ bias); 1: the SwiGLU form (N = 2F interleaved rows, y [M][F])
 };
+
+// One item of the SwiGLU reduction: token t0 + tok, interleaved rows [n, n + 16) of W (8 gate rows, then the 8 up
+// rows of the same outputs), summed over the split partials in rank order; act outputs [n / 2, n / 2 + 8).
+template <int TN>
+__device__ __forceinline__ void swiglu_item(const Params &P, const float *inbox, int split, int rpo, int grp, int tok,
+                                            int t0, int n, bool vec) {
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; j++) v[j] = 0.f;
+#pragma unroll
+    for (int q = 0; q < MAX_SPLIT; q++) {  // rank order: the same sum on every run
+        if (q < split) {
+            const float *src = inbox + (q * rpo + grp * 16) * TN + tok;
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[j] += src[j * TN];
+        }
+    }
+    if (t0 + tok >= P.M || n + 16 > P.N) return;
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        // gate and up as the plain form stores them (bias added before the one rounding), then silu_mul's arithmetic
+        const float g = bf2f(f2bf(P.bias ? v[j] + bf2f(P.bias[n + j]) : v[j]));
+        const float u = bf2f(f2bf(P.bias ? v[8 + j] + bf2f(P.bias[n + 8 + j]) : v[8 + j]));
+        o[j] = bf2f(f2bf(g / (1.f + __expf(-g)))) * u;
+    }
+    bf16 *yp = P.y + static_cast<long>(t0 + tok) * P.ldy + n / 2;
+    if (vec) {
+        uint4 w;
+        w.x = pack_bf16x2(o[0], o[1]);
+        w.y = pack_bf16x2(o[2], o[3]);
+        w.z = pack_bf16x2(o[4], o[5]);
+        w.w = pack_bf16x2(o[6], o[7]);
+        *reinterpret_cast<uint4 *>(yp) = w;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) yp[j] = f2bf(o[j]);
+    }
+}
 
 template <int TN, int STAGES>
 __global__ void __launch_bounds__(NTHREADS, 1)
@@ -84,7 +132,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int n0 = (tile % P.NT) * BW, t0 = (tile / P.NT) * TN;
     const int kb0 = rank * P.KB / split, kb1 = (rank + 1) * P.KB / split;
     const int n_units = kb1 - kb0;
-    const int rpo = rows_per_owner(split);
+    const int rpo = rows_per_owner(split, P.act);
 
     if (threadIdx.x == 0) {
         pdl_trigger();
@@ -191,13 +239,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     pdl_wait();      // y is written only after the preceding kernel completed
     {
         const int r0 = rank * rpo, r1 = min(BW, r0 + rpo);
-        const int groups = r1 > r0 ? (r1 - r0) / 8 : 0;
+        const int gsz = P.act ? 16 : 8;  // rows per item
+        const int groups = r1 > r0 ? (r1 - r0) / gsz : 0;
         const bool vec = (reinterpret_cast<uintptr_t>(P.y) & 15u) == 0 && (P.ldy & 7) == 0 &&
                          (reinterpret_cast<uintptr_t>(P.bias) & 15u) == 0;
         for (int item = threadIdx.x; item < TN * groups; item += NTHREADS) {
             const int grp = item / TN;
             const int tok = item - grp * TN;  // consecutive threads, consecutive tokens: no bank conflicts
-            const int row = r0 + grp * 8;
+            const int row = r0 + grp * gsz;
+            if (P.act) {
+                swiglu_item<TN>(P, inbox, split, rpo, grp, tok, t0, n0 + row, vec);
+                continue;
+            }
             float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int q = 0; q < MAX_SPLIT; q++) {  // rank order: the same sum on every run

@@ -537,9 +537,12 @@ bool gemm_args_ok(const void *x, int ldx, const void *w, const void *y, int ldy,
 
 template <int TN, int STAGES>
 int launch_gemm(const void *x, int ldx, const void *w, void *y, int ldy, const void *bias, int M, int N, int K,
-                GemmShape gs, int dev, cudaStream_t st) {
+                GemmShape gs, int dev, cudaStream_t st, int act = 0) {
+    // the SwiGLU form takes the split the plain form would (so it sums each output in the same order and its gate
+    // and up values are those the plain form stores); its inbox may be larger, which only matters for residency
     gemm_pick_split<TN, STAGES>(gs, dev);
-    if (gs.tiles * gs.split > 0x7fffffffL) return OUMU_ERR_UNSUPPORTED;
+    if (gs.tiles * gs.split > 0x7fffffffL || gm::Cfg<TN, STAGES>::smem_bytes(gs.split, act) > kSmemMax)
+        return OUMU_ERR_UNSUPPORTED;
     CUtensorMap tw, tx;
     int rc = make_map(&tw, w, K, N, static_cast<uint64_t>(K) * 2, gm::BK, gm::BW);
     if (rc) return rc;
@@ -554,10 +557,11 @@ int launch_gemm(const void *x, int ldx, const void *w, void *y, int ldy, const v
     P.NT = gs.nt;
     P.KB = gs.kb;
     P.split = gs.split;
+    P.act = act;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(gs.tiles * gs.split));
     cfg.blockDim = dim3(gm::NTHREADS);
-    cfg.dynamicSmemBytes = gm::Cfg<TN, STAGES>::smem_bytes(gs.split);
+    cfg.dynamicSmemBytes = gm::Cfg<TN, STAGES>::smem_bytes(gs.split, act);
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1055,6 +1059,23 @@ int oumu_gemm(const void *x, int ldx, const void *w, void *y, int ldy, const voi
     if (gs.tn == 32) return launch_gemm<32, kGemmStages32>(x, ldx, w, y, ldy, bias, M, N, K, gs, dev, st);
     if (gs.tn == 64) return launch_gemm<64, kGemmStages64>(x, ldx, w, y, ldy, bias, M, N, K, gs, dev, st);
     return launch_gemm<128, kGemmStages128>(x, ldx, w, y, ldy, bias, M, N, K, gs, dev, st);
+}
+
+int oumu_gemm_swiglu(const void *x, int ldx, const void *w_il, void *act, int ldact, const void *bias_il, int M,
+                     int F, int K, oumu_stream_t stream) {
+    if (F < 8 || F % 8 != 0 || F > (1 << 29)) return OUMU_ERR_INVALID;
+    const int N = 2 * F;
+    // the act rows are F wide: the checks of the plain form with its N, then the output's own pitch
+    if (!gemm_args_ok(x, ldx, w_il, act, N, M, N, K) || ldact < F) return OUMU_ERR_INVALID;
+    int sms = 0, dev = 0;
+    int rc = current_device(&sms);
+    if (rc) return rc;
+    OUMU_CK(cudaGetDevice(&dev));
+    const GemmShape gs = gemm_shape(M, N, K);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (gs.tn == 32) return launch_gemm<32, kGemmStages32>(x, ldx, w_il, act, ldact, bias_il, M, N, K, gs, dev, st, 1);
+    if (gs.tn == 64) return launch_gemm<64, kGemmStages64>(x, ldx, w_il, act, ldact, bias_il, M, N, K, gs, dev, st, 1);
+    return launch_gemm<128, kGemmStages128>(x, ldx, w_il, act, ldact, bias_il, M, N, K, gs, dev, st, 1);
 }
 
 }  // extern "C"

@@ -92,14 +92,25 @@ class _Init:
 
 class Lin:
     """y = x W^T (+ b), weight [n][k] bf16 (src/model.rs:27-45). `tc`: through this library's tensor-core GEMM
-    (oumu_gemm) instead of cuBLAS."""
+    (oumu_gemm) instead of cuBLAS. `swiglu` (with tc, for an MLP's gate|up projection): the call writes the SwiGLU
+    activation [rows][n/2] instead (oumu_gemm_swiglu), the weight kept with its rows interleaved for it."""
 
-    def __init__(self, ini, n, k, bias, tc=False):
+    def __init__(self, ini, n, k, bias, tc=False, swiglu=False):
         self.w = ini.w(n, k)
         self.b = ini.w(n) if bias else None
         self.tc = tc
+        self.swiglu = bool(tc and swiglu)
+        if self.swiglu:
+            self.w = ops.swiglu_interleave(self.w)
+            self.b = ops.swiglu_interleave(self.b) if self.b is not None else None
+
+    def standard_weight(self):
+        """The weight in [n][k] row order (the gate rows, then the up rows, for a SwiGLU projection)."""
+        return ops.swiglu_deinterleave(self.w) if self.swiglu else self.w
 
     def __call__(self, x, out):
+        if self.swiglu:
+            return ops.gemm_swiglu(x, self.w, out, bias_il=self.b)
         if self.tc:
             return ops.gemm(x, self.w, out, bias=self.b)
         if self.b is None:
@@ -117,7 +128,7 @@ class Tf:
     def __init__(self, ini, n, h, ffn, rope, slots=0, maxlen=0, tc=()):
         self.h, self.ffn, self.rope = h, ffn, rope
         self.layers = [dict(ln1=ini.norm(h), qkv=Lin(ini, QKV, h, False, "qkv" in tc), o=Lin(ini, h, QW, False, "o" in tc),
-                            ln2=ini.norm(h), gu=Lin(ini, 2 * ffn, h, False, "gu" in tc),
+                            ln2=ini.norm(h), gu=Lin(ini, 2 * ffn, h, False, "gu" in tc, "swiglu" in tc),
                             down=Lin(ini, h, ffn, False, "down" in tc)) for _ in range(n)]
         self.norm = ini.norm(h)
         shape = (slots, NK, maxlen, HD)
@@ -139,7 +150,8 @@ class Engine:
     # programmatic dependent launch through the norm / SwiGLU kernels between them, each GEMM streams its weights
     # while the preceding kernel finishes: 4.68 ms per captured step against 4.77 ms on cuBLAS (32 takes, the same
     # B200). lm_tc=() selects cuBLAS.
-    LM_TC = ("qkv", "o", "gu", "down")
+    # "swiglu": the gate|up GEMM writes the SwiGLU activation itself (oumu_gemm_swiglu), one launch per layer fewer.
+    LM_TC = ("qkv", "o", "gu", "down", "swiglu")
 
     def __init__(self, B, maxlen=4096, timesteps=10, base_layers=28, res_layers=8, enc_layers=4, dit_layers=4,
                  cfg=2.0, max_steps=256, min_len=2, seed=0, device="cuda", lm_tc=LM_TC):
@@ -256,8 +268,11 @@ class Engine:
         l = tf.layers[li]
         l["o"](sc["att"], sc["tmp"])
         ops.rmsnorm(x, l["ln2"], sc["xn"], EPS, d=sc["tmp"])
-        l["gu"](sc["xn"], sc["gu"])
-        ops.silu_mul(sc["gu"], sc["act"])
+        if l["gu"].swiglu:  # gate|up projection and SwiGLU in one launch
+            l["gu"](sc["xn"], sc["act"])
+        else:
+            l["gu"](sc["xn"], sc["gu"])
+            ops.silu_mul(sc["gu"], sc["act"])
         l["down"](sc["act"], sc["tmp"])
         last = li + 1 == len(tf.layers)
         ops.rmsnorm(x, tf.norm if last else tf.layers[li + 1]["ln1"], out if last else sc["xn"], EPS, d=sc["tmp"])

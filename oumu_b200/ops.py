@@ -235,6 +235,34 @@ def gemm(x, w, y, bias=None):
     return y
 
 
+def swiglu_interleave(w):
+    """The gate|up weight [2F][...] (or bias [2F]) with its rows interleaved in groups of 8, the layout
+    oumu_gemm_swiglu reads: rows [16j, 16j + 8) = gate rows [8j, 8j + 8), rows [16j + 8, 16j + 16) = up rows."""
+    F = w.shape[0] // 2
+    if w.shape[0] != 2 * F or F % 8:
+        raise ValueError("swiglu_interleave: 2F rows with F a multiple of 8")
+    return w.reshape(2, F // 8, 8, *w.shape[1:]).transpose(0, 1).reshape(w.shape).contiguous()
+
+
+def swiglu_deinterleave(w_il):
+    """The inverse of swiglu_interleave: [gate | up] rows again."""
+    F = w_il.shape[0] // 2
+    return w_il.reshape(F // 8, 2, 8, *w_il.shape[1:]).transpose(0, 1).reshape(w_il.shape).contiguous()
+
+
+def gemm_swiglu(x, w_il, act, bias_il=None):
+    """act[M][F] = bf16(bf16(silu(gate)) * up) of the gate|up projection x . W^T, one launch (oumu_gemm_swiglu);
+    w_il [2F][K] (and bias_il) interleaved by swiglu_interleave. Bit-identical to gemm into [M][2F] + silu_mul."""
+    M, K = x.shape
+    F = w_il.shape[0] // 2
+    if (w_il.shape[1] != K or x.stride(1) != 1 or act.stride(1) != 1 or not w_il.is_contiguous()
+            or tuple(act.shape) != (M, F)):
+        raise ValueError("gemm_swiglu: x [M][K] and act [M][F] with unit column stride, w_il [2F][K] contiguous")
+    _lib.call("oumu_gemm_swiglu", _p(x), x.stride(0), _p(w_il), _p(act), act.stride(0), _p(bias_il), M, F, K,
+              _stream())
+    return act
+
+
 def attn_prefill_kv(qkv, out, kc, vc, T, slots, nq, nk, hd, maxlen, scale):
     """Causal prefill of one prompt + its k/v into every take slot, one launch (oumu_attn_prefill_kv): replaces
     kv_write + attn_full (src/model.rs:553-567) and kv_replicate (src/model.rs:705-717)."""

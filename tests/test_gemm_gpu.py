@@ -127,3 +127,44 @@ def test_gemm_rejects_bad_shapes(cuda):
     y = torch.empty((8, 16), dtype=torch.bfloat16, device="cuda")
     with pytest.raises(_lib.OumuError):
         ops.gemm(x, w, y)  # K not a multiple of 64
+
+
+# (M, F, K): the LM's gate|up at 32 and 64 takes, one-tile and one-K-block shapes, and shapes whose K split is 6 or
+# 7 (owner row ranges the SwiGLU form rounds to whole 16-row groups), with 32, 64 and 128-token tiles
+SWIGLU_SHAPES = [(32, 6144, 2048), (64, 6144, 2048), (1, 8, 64), (5, 24, 128), (48, 200, 4096), (32, 1280, 2048),
+                 (32, 1536, 2048), (100, 1280, 2048), (704, 1024, 1024), (33, 1000, 512)]
+
+
+@pytest.mark.parametrize("M,F,K", SWIGLU_SHAPES)
+def test_gemm_swiglu_bit_identical_to_gemm_then_silu_mul(cuda, M, F, K):
+    """oumu_gemm_swiglu (gate|up projection with the SwiGLU activation in its epilogue) against the two launches it
+    replaces, oumu_gemm into [gate | up] and oumu_silu_mul (kernels/voxcpm.cu:92-99): bit-identical, with and
+    without a bias, into a row-strided output whose padding it leaves alone."""
+    x, w = rnd((M, K), 4), rnd((2 * F, K), 5, 0.02)
+    bias = rnd((2 * F,), 6, 0.1)
+    w_il = ops.swiglu_interleave(w)
+    assert torch.equal(ops.swiglu_deinterleave(w_il), w)
+    for b in (None, bias):
+        gu = torch.empty((M, 2 * F), dtype=torch.bfloat16, device="cuda")
+        ops.gemm(x, w, gu, bias=b)
+        want = torch.empty((M, F), dtype=torch.bfloat16, device="cuda")
+        ops.silu_mul(gu, want)
+        buf = torch.full((M, F + 8), 7.0, dtype=torch.bfloat16, device="cuda")
+        ops.gemm_swiglu(x, w_il, buf[:, :F], bias_il=None if b is None else ops.swiglu_interleave(b))
+        torch.cuda.synchronize()
+        assert torch.equal(buf[:, :F], want), (M, F, K, b is not None, float((buf[:, :F].float() - want.float()).abs().max()))
+        assert bool((buf[:, F:] == 7.0).all())
+    assert ops.device_error() == 0
+
+
+def test_gemm_swiglu_rejects_bad_shapes(cuda):
+    from oumu_b200 import _lib
+    x = rnd((8, 128), 1)
+    w = rnd((24, 128), 2)  # F = 12: not a multiple of 8
+    act = torch.empty((8, 12), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.OumuError):
+        _lib.call("oumu_gemm_swiglu", x.data_ptr(), 128, w.data_ptr(), act.data_ptr(), 12, None, 8, 12, 128, None)
+    w = rnd((32, 128), 2)
+    act = torch.empty((8, 16), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_lib.OumuError):  # output pitch below F
+        _lib.call("oumu_gemm_swiglu", x.data_ptr(), 128, w.data_ptr(), act.data_ptr(), 8, None, 8, 16, 128, None)

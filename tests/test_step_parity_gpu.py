@@ -55,7 +55,8 @@ def _load_state(dst, src):
         getattr(dst, name).copy_(getattr(src, name))
 
 
-@pytest.mark.parametrize("lm_tc", [(), ("qkv", "o", "gu", "down")], ids=["cublas_gemms", "library_gemms"])
+@pytest.mark.parametrize("lm_tc", [(), ("qkv", "o", "gu", "down"), ("qkv", "o", "gu", "down", "swiglu")],
+                         ids=["cublas_gemms", "library_gemms", "library_gemms_fused_swiglu"])
 def test_decoding_step_matches_the_reference_kernels(cuda, lm_tc):
     from oracle import refkern
     if not refkern.available():
@@ -113,3 +114,26 @@ def test_decoding_step_matches_the_reference_kernels(cuda, lm_tc):
     print("step parity over", STEPS, "steps: worst patch rel-L2", f"{worst.pop('patch'):.2e};",
           "worst ratio to the reference's one-ulp floor:", {k: f"{v:.2f}" for k, v in worst.items()},
           "stop flags", stops[-1])
+
+
+def test_fused_swiglu_step_is_bit_identical(cuda):
+    """The engine's default LM path (the gate|up GEMM writing the SwiGLU activation itself, oumu_gemm_swiglu) against
+    the same engine with the GEMM and silu_mul as two launches: same seed, same state, three steps, every output
+    and state bit for bit."""
+    kw = dict(maxlen=MAXLEN, max_steps=16, min_len=2, seed=0)
+    a = engine.Engine(B, lm_tc=("qkv", "o", "gu", "down", "swiglu"), **kw)
+    b = engine.Engine(B, lm_tc=("qkv", "o", "gu", "down"), **kw)
+    assert a.base.layers[0]["gu"].swiglu and not b.base.layers[0]["gu"].swiglu
+    assert torch.equal(a.base.layers[3]["gu"].standard_weight(), b.base.layers[3]["gu"].w)
+    for e in (a, b):
+        e.prime([L0, L0 + 17, L0 + 40, L0 + 5], seed=1)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    for n in range(3):
+        noise = torch.randn((B, engine.PATCH), generator=g, device="cuda").to(torch.bfloat16)
+        for e in (a, b):
+            e.noise.copy_(noise)
+            e.step()
+        torch.cuda.synchronize()
+        for what in ("x", "cond", "lm_h", "res_h", "stop_l", "q", "patches", "stop", "lens", "ctr"):
+            assert torch.equal(getattr(a, what), getattr(b, what)), f"step {n}: {what} differs"
