@@ -143,8 +143,35 @@ __global__ void __launch_bounds__(nthreads(NWG), 1)
     // allocated only after it has completed (a kernel that takes all 512 columns before its predecessor ends could
     // hold columns that predecessor has yet to allocate), and the next kernel is let in only once the columns are
     // held (so none of its CTAs can take them first).
+    // The producer's first unit goes out as soon as the preceding kernel has completed, ahead of the TMEM allocation
+    // and the block-wide set-up (the padding below writes other rows of the slots); the rest once the warpgroups run.
+    // (All the slots' units issued that early held the set-up back: 15.2 against 12.1 us at the DiT shape.)
+    const uint32_t tx = static_cast<uint32_t>(NBOX * (P.qrows + 2 * P.krows) * 128);
+    auto issue = [&](int k) {
+        int n, qh0, kh0;
+        unit_heads(P, c + k * grid, n, qh0, kh0);
+        const uint32_t dst = slot_s(k), fb = bar(B_FULL + k % P.nslot);
+        mbar_expect_tx(fb, tx);
+#pragma unroll
+        for (int b = 0; b < NBOX; b++) {
+            tma_load_3d(dst + b * P.qbox, &tq, fb, b * 64, qh0, n * P.seq);
+            tma_load_3d(dst + koff + b * P.kbox, &tkv, fb, b * 64, P.nq + kh0, n * P.seq);
+            tma_load_3d(dst + voff + b * P.kbox, &tkv, fb, b * 64, P.nq + P.nk + kh0, n * P.seq);
+        }
+    };
+    const int first = nunits < 1 ? nunits : 1;
+    int last_k[NSLOT_MAX];  // producer: the last unit loaded into each slot (-1: none)
     if (warp == 0) {
         pdl_wait();
+        if (lane == 0) {
+            tma_prefetch_desc(&tq);
+            tma_prefetch_desc(&tkv);
+            tma_prefetch_desc(&tout);
+#pragma unroll
+            for (int i = 0; i < NSLOT_MAX; i++) last_k[i] = i < first ? i : -1;
+            for (int k = 0; k < first; k++) issue(k);
+        }
+        __syncwarp();
         tmem_alloc(bar(B_TMEM), 512);
         tmem_relinquish();
     }
@@ -177,33 +204,17 @@ __global__ void __launch_bounds__(nthreads(NWG), 1)
     const uint32_t tmem = *tmem_slot;
     if (threadIdx.x == 0) pdl_trigger();
 
-    int last_k[NSLOT_MAX];  // producer: the last unit loaded into each slot (-1: none)
     if (warp == 0) {
-        // ------------------------------ TMA producer ------------------------------
+        // ------------------------------ TMA producer: the units after the first ------------------------------
         if (lane == 0) {
-#pragma unroll
-            for (int i = 0; i < NSLOT_MAX; i++) last_k[i] = -1;
-            tma_prefetch_desc(&tq);
-            tma_prefetch_desc(&tkv);
-            tma_prefetch_desc(&tout);
-            const uint32_t tx = static_cast<uint32_t>(NBOX * (P.qrows + 2 * P.krows) * 128);
-            for (int k = 0; k < nunits; k++) {
+            for (int k = first; k < nunits; k++) {
                 const int s = k % P.nslot;
-                if (k >= P.nslot && !mbar_wait(bar(B_EMPTY + s), ((k / P.nslot) - 1) & 1)) {
+                if (!mbar_wait(bar(B_EMPTY + s), ((k / P.nslot) - 1) & 1)) {
                     *abort_flag = 1;
                     break;
                 }
                 if (*abort_flag) break;
-                int n, qh0, kh0;
-                unit_heads(P, c + k * grid, n, qh0, kh0);
-                const uint32_t dst = slot_s(k), fb = bar(B_FULL + s);
-                mbar_expect_tx(fb, tx);
-#pragma unroll
-                for (int b = 0; b < NBOX; b++) {
-                    tma_load_3d(dst + b * P.qbox, &tq, fb, b * 64, qh0, n * P.seq);
-                    tma_load_3d(dst + koff + b * P.kbox, &tkv, fb, b * 64, P.nq + kh0, n * P.seq);
-                    tma_load_3d(dst + voff + b * P.kbox, &tkv, fb, b * 64, P.nq + P.nk + kh0, n * P.seq);
-                }
+                issue(k);
                 last_k[s] = k;
             }
         }
