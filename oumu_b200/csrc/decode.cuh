@@ -412,6 +412,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int B = P.B, nk = P.nk, G = P.nq / P.nk;
 
+    // the tensor maps' descriptors are fetched while warp 0 scans the lengths
+    if (threadIdx.x == PRODUCER * 32) {
+        tma_prefetch_desc(&tk);
+        tma_prefetch_desc(&tv);
+    }
     // ---- per-take lengths and the tile prefix over takes (warp 0) ----
     if (warp == 0) {
         const int per = (B + 31) / 32, s0 = lane * per;
@@ -480,8 +485,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         int st = 0;
         uint32_t use = 0;
         if (lane == 0) {
-            tma_prefetch_desc(&tk);
-            tma_prefetch_desc(&tv);
             TileIt it;
             it.seek(ta, pre, Ls, B);
             const long tend = DROP && c == 0 ? tb - 1 : tb;
