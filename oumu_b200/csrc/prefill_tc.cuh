@@ -426,12 +426,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 m = mt;
             }
             const float mref = m == -INFINITY ? 0.f : m;
-            // p = 2^(s * sl2 - mref) per column, summed in eight independent chains (column c into chain c % 8),
-            // the scaling and the sums two columns per packed instruction
+            // P_j goes into buffer j & 1 once PV_{j-2} has read it (issued two tiles back, so this wait is short).
+            // A wait that times out here ends the loop at the next tile's vote.
+            if (j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_PDONE0 + (j & 1)), ((j >> 1) - 1) & 1));
+            if (!ok) continue;
+            // p = 2^(s * sl2 - mref) per column, summed in eight independent chains (column c into chain c % 8), and
+            // straight away this half of P row r (keys cb .. cb + 63) as bf16 pairs for TMEM buffer j & 1: hi (p
+            // truncated to bf16, its upper 16 bits taken with a byte permute) in columns [32wg, 32wg + 32), lo (the
+            // exact remainder p - hi rounded to bf16; hi + lo keeps ~16 bits of p) in [64 + 32wg, ...). One loop, so
+            // the exponentials of a pair (multi-function unit) overlap the packing of the pairs before it (ALU); the
+            // scaling, the sums and the remainders two columns per packed instruction. sr[k] takes the k-th hi pair
+            // in place (pair k reads sr[2k], sr[2k + 1], which no earlier pair has written).
             float2 rs2[4];
 #pragma unroll
             for (int k = 0; k < 4; k++) rs2[k] = make_float2(0.f, 0.f);
             const float2 sl2v = make_float2(sl2, sl2), nmref = make_float2(-mref, -mref);
+            uint32_t lw[32];
 #pragma unroll
             for (int i = 0; i < 32; i++) {
                 const float2 x = fma2(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sl2v,
@@ -439,16 +449,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 // one pair in eight on the FMA pipe, the rest on the multi-function unit, which bounds this loop
                 const float2 p = (i % 8) == 0 ? exp2_poly2(x) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
                 rs2[i & 3] = add2(rs2[i & 3], p);
-                sr[2 * i] = __float_as_uint(p.x);
-                sr[2 * i + 1] = __float_as_uint(p.y);
+                const uint32_t u0 = __float_as_uint(p.x), u1 = __float_as_uint(p.y);
+                const float2 lo = sub2(p, make_float2(__uint_as_float(u0 & 0xffff0000u),
+                                                      __uint_as_float(u1 & 0xffff0000u)));
+                lw[i] = pack_bf16x2(lo.x, lo.y);
+                sr[i] = __byte_perm(u0, u1, 0x7632);
             }
             const float rs = ((rs2[0].x + rs2[0].y) + (rs2[1].x + rs2[1].y)) +
                              ((rs2[2].x + rs2[2].y) + (rs2[3].x + rs2[3].y));
             l = l * alpha + rs;
-            // P_j goes into buffer j & 1 once PV_{j-2} has read it; O may be rescaled once PV_{j-1} has completed.
-            // A wait that times out here ends the loop at the next tile's vote.
-            if (j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_PDONE0 + (j & 1)), ((j >> 1) - 1) & 1));
-            if (ok && j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+            const uint32_t tPb = tmem + lane_off + C::P_COL + (j & 1) * 128;
+            tmem_st32(tPb + wg * 32, sr);
+            tmem_st32(tPb + 64 + wg * 32, lw);
+            // O may be rescaled once PV_{j-1} has completed, and must be before PV_j starts (after PFULL)
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
                 ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE), (j - 1) & 1));
                 if (ok) {
                     tc_fence_after();
@@ -461,30 +475,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         for (int k = 0; k < 32; k++) orow[k] = __float_as_uint(__uint_as_float(orow[k]) * alpha);
                         tmem_st32(tO + wg * OH + c, orow);
                     }
-                    tc_wait_st();
                 }
             }
-            if (!ok) continue;
-            // this half of P row r (keys cb .. cb + 63) -> TMEM buffer j & 1 as bf16 pairs: hi (p truncated) in
-            // columns [32wg, 32wg + 32), lo (the rest) in [64 + 32wg, ...); sr[k] takes the k-th hi pair in place
-            uint32_t lw[32];
-#pragma unroll
-            for (int k = 0; k < 32; k++) {
-                // hi: p truncated to bf16 (its upper 16 bits, taken with a byte permute instead of a conversion);
-                // lo: the exact remainder p - hi rounded to bf16. hi + lo keeps ~16 bits of p.
-                const uint32_t u0 = sr[2 * k], u1 = sr[2 * k + 1];
-                const uint32_t hw = __byte_perm(u0, u1, 0x7632);
-                const float2 lo = sub2(make_float2(__uint_as_float(u0), __uint_as_float(u1)),
-                                       make_float2(__uint_as_float(u0 & 0xffff0000u), __uint_as_float(u1 & 0xffff0000u)));
-                lw[k] = pack_bf16x2(lo.x, lo.y);
-                sr[k] = hw;
-            }
-            const uint32_t tPb = tmem + lane_off + C::P_COL + (j & 1) * 128;
-            tmem_st32(tPb + wg * 32, sr);
-            tmem_st32(tPb + 64 + wg * 32, lw);
             tc_wait_st();
             tc_fence_before();
             __syncwarp();
+            if (!ok) continue;
             if (lane == 0) mbar_arrive(bar(B_PFULL));
         }
         // O is final once the last P.V has completed: waited on that P buffer's barrier, whose phase before it (the
