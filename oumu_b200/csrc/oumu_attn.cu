@@ -18,6 +18,7 @@
 #include "full_small.cuh"
 #include "gemm_tc.cuh"
 #include "prefill_tc.cuh"
+#include "prefill_pp.cuh"
 #include "small_tc.cuh"
 #include "step_glue.cuh"
 
@@ -61,6 +62,7 @@ constexpr int kMaxDevices = 64;
 // inbox). At 32 tokens, 8 stages keep 160 KB of weights in flight per SM: a GEMM whose tiles occupy only part of the
 // SMs (gate|up on 96) still streams at the HBM rate (captured decoding step: 4.69 -> 4.55 ms against 4 stages).
 constexpr int kGemmStages32 = 8, kGemmStages64 = 4, kGemmStages128 = 3;
+constexpr int kPrefillPairMinSeq = 4096;  // sequences from this length take the ping-pong prefill kernel
 
 constexpr int kSmemMax = 227 * 1024;
 
@@ -96,6 +98,10 @@ int current_device(int *sms) {
         OUMU_CK(cudaFuncSetAttribute(dec::k_attn_decode<128, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kSmemMax));
         OUMU_CK(cudaFuncSetAttribute(dec::k_attn_decode<64, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(pp::k_attn_prefill_pp<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemMax));
+        OUMU_CK(cudaFuncSetAttribute(pp::k_attn_prefill_pp<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kSmemMax));
         OUMU_CK(cudaFuncSetAttribute(pf::k_attn_prefill<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      pf::Cfg<128>::SMEM));
@@ -460,6 +466,18 @@ int launch_prefill(const void *qkv, void *out, int rows, int seq, int causal, in
     int sms = 0;
     int rc2 = current_device(&sms);
     if (rc2) return rc2;
+    // Long sequences without the KV epilogue: two query tiles per CTA in ping-pong (pp::k_attn_prefill_pp), whose
+    // output is bit-identical. Measured on a B200 (16 q / 2 kv heads, hd 128, causal): T = 4096 92 against 99 us,
+    // T = 16384 1.31 against 1.43 ms; at T = 2048 the pairs' causal chains on half as many CTAs lose (50 against
+    // 31 us).
+    if (slots == 0 && seq >= kPrefillPairMinSeq) {
+        const int pairs = (qtiles + 1) / 2;
+        // more than half an SM's shared memory, so that no two CTAs (each allocating all 512 TMEM columns) share an SM
+        const int smem = std::max(pp::Cfg<HD>::SMEM, 120 * 1024);
+        OUMU_CK(launch_k(pp::k_attn_prefill_pp<HD>, dim3(nq, pairs, nseq), dim3(pp::NTHREADS), smem, st,
+                         tm, static_cast<bf16 *>(out), seq, causal, nq, nk, scale * 1.4426950408889634f));
+        return OUMU_OK;
+    }
     const pf::CopyPlan plan = prefill_copy_plan(HD, seq, causal, nq, nk, nseq, slots, sms);
     dim3 grid(nq, qtiles + (plan.planned ? 1 : 0), nseq);
     OUMU_CK(launch_k(pf::k_attn_prefill<HD>, grid, dim3(pf::NTHREADS), pf::Cfg<HD>::SMEM, st, tm,

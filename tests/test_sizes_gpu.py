@@ -384,3 +384,19 @@ def test_decode_one_long_take(cuda, L):
     qkv, kc, vc, ln = decode_case(B, [L], maxlen, seed=41)
     att, _ = run_decode(qkv, kc, vc, ln, B, maxlen)
     gc.assert_close(u16(att), oracle_decode(qkv, kc, vc, [L], B, maxlen), f"one take, L={L}")
+
+
+@pytest.mark.parametrize("nseq,seq,causal,hd,nq,nk", [(2, 4100, 1, 64, 2, 1), (1, 4352, 0, 128, 2, 2),
+                                                       (1, 4096, 1, 128, 4, 2)])
+def test_long_prefill_pairs_vs_oracle(cuda, nseq, seq, causal, hd, nq, nk):
+    # sequences of 4096 positions and more take the two-tiles-per-CTA kernel (pp::k_attn_prefill_pp): ragged last
+    # tiles reaching into the next sequence's rows, an odd number of query tiles (a CTA with one tile), non-causal
+    # rows over every key tile, hd 64 and 128, one and two q heads per kv head
+    rows, W = nseq * seq, (nq + 2 * nk) * hd
+    qkv = rand_bf16((rows, W), 130 + seq + causal)
+    out = torch.zeros((rows, nq * hd), dtype=torch.bfloat16, device="cuda")
+    ops.attn_full(qkv, out, rows, seq, causal, nq, nk, hd, hd ** -0.5)
+    torch.cuda.synchronize()
+    ref = cpu.attn_full(u16(qkv), rows, seq, causal, nq, nk, hd, hd ** -0.5)
+    gc.assert_close(u16(out), ref, f"{nseq} x {seq} causal={causal} hd={hd}")
+    assert ops.device_error() == 0
