@@ -400,7 +400,7 @@ int launch_small_tc(const void *qkv, void *out, int rows, int seq, int causal, i
 // whichever CTA that does not load the tile is expected to be free first: query tile qt is busy until ~kPfFixedUs + (qt + 1) * kPfTileUs, the copy CTA from kPfCopyStartUs, and each
 // group costs its stores at kPfStoreGBs per SM, plus a load of the tile for the first group a CTA takes of it.
 constexpr double kPfFixedUs = 5.0, kPfTileUs = 1.6, kPfCopyStartUs = 1.5, kPfLoadUs = 0.5;
-constexpr double kPfStoreGBs = 85.0, kPfLoopBytes = 256.0 * 1024;
+constexpr double kPfStoreGBs = 85.0, kPfLoopBytes = 384.0 * 1024;
 
 pf::CopyPlan prefill_copy_plan(int hd, int seq, int causal, int nq, int nk, int nseq, int slots, int sms) {
     pf::CopyPlan plan;
